@@ -1,0 +1,170 @@
+"""Forward / backward / autograd API — drop-in for the reference's ops layer.
+
+Mirrors ops/attention_forward.py:23-167, ops/attention_backward.py:19-76 and
+ops/attention_func.py:20-125: same names, arguments, shapes and return
+values.  The work is done by the sm_100a kernels in libffa_b200.so; there is
+no Triton path and no CPU fallback (CPU tensors raise).
+
+Numerics: fp16/bf16 inputs are consumed as-is by the tensor cores with fp32
+accumulation.  fp32 inputs are rounded to bf16 (or to ``compute_dtype`` when
+that is fp16/bf16) before the kernels run and the result is cast back to
+fp32, so fp32 callers get bf16-level accuracy.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+from torch.autograd import Function
+
+from . import _lib
+from .config import AttentionConfig
+from .utils import auto_select_block_size, maybe_unsqueeze_head
+
+_KERNEL_DTYPES = (torch.float16, torch.bfloat16)
+SUPPORTED_HEAD_DIMS = (64, 128)
+
+
+def kernel_dtype(t: torch.Tensor, compute_dtype: Optional[torch.dtype] = None) -> torch.dtype:
+    if t.dtype in _KERNEL_DTYPES:
+        return t.dtype
+    if compute_dtype in _KERNEL_DTYPES:
+        return compute_dtype
+    return torch.bfloat16
+
+
+def _tma_ready(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Cast to the kernel dtype and make the layout TMA-addressable
+    (unit stride in D, 16-byte aligned base and outer strides)."""
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if (t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:-1]) or t.data_ptr() % 16
+            or any(s == 0 for s in t.stride()[:-1])):
+        t = t.contiguous()
+    return t
+
+
+def _strides_bhs(t: torch.Tensor):
+    return _lib.i64arr(t.stride(0), t.stride(1), t.stride(2))
+
+
+def flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float, causal: bool = False,
+              q_offset: int = 0, window: Optional[int] = None, softcap: Optional[float] = None,
+              block_mask: Optional[torch.Tensor] = None, mask_block: Tuple[int, int] = (64, 64),
+              compute_dtype: Optional[torch.dtype] = None, want_lse: bool = True
+              ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Run the sm_100a forward kernel on 4-D [B, H, S, D] tensors.
+
+    Returns (O in the kernel dtype with q's stride order, LSE [B, Hq, Sq] fp32).
+    """
+    _lib.require_cuda(q, k, v)
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    if k.shape[0] != B or v.shape[:3] != k.shape[:3] or k.shape[3] != D or v.shape[3] != D:
+        raise ValueError(f"incompatible q/k/v shapes {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    if Hq % Hkv != 0:
+        raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
+    if D not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim {D} not supported by the sm_100a forward kernel (supported: {SUPPORTED_HEAD_DIMS})")
+    dt = kernel_dtype(q, compute_dtype)
+    q = _tma_ready(q, dt)
+    k = _tma_ready(k, dt)
+    v = _tma_ready(v, dt)
+    o = torch.empty_like(q)  # keeps q's stride order when q is dense
+    lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device) if want_lse else None
+    bm_ptr, n_br, n_bc = None, 0, 0
+    if block_mask is not None:
+        bm = block_mask.to(device=q.device, dtype=torch.uint8).contiguous()
+        n_br, n_bc = bm.shape
+        bm_ptr = bm.data_ptr()
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        st = lib.ffa_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else None,
+            _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D,
+            _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o),
+            float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),
+            bm_ptr, n_br, n_bc, int(mask_block[0]), int(mask_block[1]),
+            _lib.err_word(q.device).data_ptr(), _lib.stream_of(q))
+    _lib.check(st, "ffa_fwd")
+    if block_mask is not None:
+        bm.record_stream(torch.cuda.current_stream(q.device))
+    if _lib.sync_check_enabled():
+        _lib.check_device_errors(q.device)
+    return o, lse
+
+
+def fastest_flash_attn_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    config: Optional[AttentionConfig] = None,
+    *,
+    scale: Optional[float] = None,
+    causal: bool = False,
+    block_size: Optional[int] = None,
+    block_mask: Optional[torch.Tensor] = None,
+    softcap: Optional[float] = None,
+    sliding_window: Optional[int] = None,
+    two_pass: bool = False,
+    compute_dtype: Optional[torch.dtype] = None,
+    num_kv_heads: Optional[int] = None,
+    kv_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+    return_lse: bool = False,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Forward attention (ops/attention_forward.py:23-167).
+
+    q [B,S_q,D] or [B,H_q,S_q,D]; k/v [B,S_kv,D] or [B,H_kv,S_kv,D].
+    Returns (output shaped like q, LSE [B,H,S_q,1] fp32 natural log or None).
+    GQA/MQA (H_q a multiple of H_kv) is handled natively without repeating
+    K/V; ``num_kv_heads`` is accepted for compatibility.  ``two_pass`` needs
+    no second pass here: the kernel's LSE is already exact.
+    """
+    if config is not None:  # attention_forward.py:66-73
+        causal = config.causal
+        softcap = config.softcap
+        sliding_window = config.sliding_window
+        two_pass = config.two_pass
+        compute_dtype = config.compute_dtype
+        num_kv_heads = config.num_kv_heads
+        return_lse = config.return_lse
+
+    in_dtype = q.dtype
+    q, k, v, squeezed = maybe_unsqueeze_head(q, k, v)
+    B, H_q, S_q, D = q.shape
+
+    q_offset = 0
+    if kv_cache is not None:  # attention_forward.py:80-89: cache is prepended, queries sit at the end
+        k_cache, v_cache = kv_cache
+        if k_cache.dim() == 3:
+            k_cache = k_cache.unsqueeze(1)
+            v_cache = v_cache.unsqueeze(1)
+        k = torch.cat([k_cache.to(k.dtype), k], dim=2)
+        v = torch.cat([v_cache.to(v.dtype), v], dim=2)
+        q_offset = k.size(2) - S_q
+    S_kv = k.size(2)
+
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+
+    if block_size is None:
+        if config is not None:
+            bq, bkv = config.resolve_block_sizes(S_q, S_kv, D)
+        else:
+            bq = bkv = auto_select_block_size(S_q, S_kv, D)
+    else:
+        bq = bkv = block_size
+
+    o, lse = flash_fwd(q, k, v, scale=scale, causal=causal, q_offset=q_offset, window=sliding_window,
+                       softcap=softcap, block_mask=block_mask, mask_block=(bq, bkv),
+                       compute_dtype=compute_dtype, want_lse=return_lse)
+    if o.dtype != in_dtype:
+        o = o.to(in_dtype)
+    if lse is not None:
+        lse = lse.unsqueeze(-1)
+    if squeezed:
+        o = o.squeeze(1)
+        if lse is not None:
+            lse = lse.squeeze(1)
+    return o, lse

@@ -1,0 +1,525 @@
+// Prefill / training forward attention for B200 (sm_100a).
+//
+// Replaces the reference's forward kernels (kernels/cpu_reference.py:132
+// flash_attn_cpu_forward, kernels/cpu_fa4.py:219 fa4_forward and the Triton
+// kernels in kernels/triton_fwd.py / triton_ffpa.py) behind ffa_fwd().
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and walks the key
+// tiles (128 keys each) its masks leave active:
+//   warp 8      TMA producer: Q once, then K_j / V_j into a ring of smem slots
+//   warp 9      MMA issuer:   S_t = Q_t K_j^T (smem x smem -> TMEM),
+//                             O_t += P_t V_j  (P from TMEM x V from smem)
+//   warps 0-3   softmax for query tile 0, warps 4-7 for query tile 1: each
+//               thread owns one query row (= one TMEM lane), reads its S row,
+//               applies scale / softcap / masks, runs the online softmax in
+//               base 2 and writes P (16-bit) back over S in TMEM.
+// The two tiles ping-pong: while one softmax group works on its scores the
+// tensor core runs the other tile's P·V and next Q·K^T.
+// Rescaling of O is lazy: the running max only moves (and O in TMEM is
+// rescaled) when a row's max grows by more than 2^8; the result is exact
+// because numerator and denominator always share the same stale max.
+// TMEM columns: [0,128) S_0/P_0, [128,256) S_1/P_1, [256,384) O_0, [384,512) O_1.
+#include "ffa_common.cuh"
+#include "ffa_host.h"
+
+namespace ffa {
+
+constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
+constexpr int FWD_NQT = 2;    // query tiles per CTA
+constexpr int FWD_BN = 128;   // keys per key tile
+constexpr int FWD_THREADS = 320;
+constexpr int FWD_WARP_LOAD = 8;
+constexpr int FWD_WARP_MMA = 9;
+constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block mask filters them
+constexpr float RESCALE_LOG2 = 8.0f;
+
+template <int D>
+struct FwdCfg {
+  static constexpr int TILE = FWD_BM * D * 2;  // bytes of one 128 x D 16-bit tile
+  static constexpr int NBUF = (D == 64) ? 8 : 4;
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = FWD_NQT * TILE;
+  static constexpr int BAR_OFF = KV_OFF + NBUF * TILE;
+  static constexpr int LIST_OFF = BAR_OFF + 512;
+  static constexpr int SMEM = LIST_OFF + FWD_MAX_LIST * 2 + 1024;  // + alignment slack
+};
+
+struct FwdParams {
+  void* o;
+  float* lse;
+  int64_t o_sb, o_sh, o_ss;
+  int B, Hq, Hkv, Sq, Skv, q_offset;
+  int n_qblk;
+  float scale_log2;   // scale * log2(e)
+  float sc_pre;       // scale / softcap
+  float sc_post;      // softcap * log2(e)
+  int use_softcap;
+  int causal, window;
+  const uint8_t* block_mask;
+  int n_br, n_bc, mask_bq, mask_bkv;
+  ErrCtx ec;
+};
+
+struct FwdBars {
+  uint64_t q_full;
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done[2];
+  uint64_t drain;
+  uint64_t kv_full[8];
+  uint64_t kv_empty[8];
+  uint32_t tmem_base;
+  int abort;
+  int n_tiles;
+  int j_lo;
+  int use_list;
+};
+
+enum : uint32_t {
+  SITE_FWD_Q = 0x101,
+  SITE_FWD_KV_EMPTY = 0x102,
+  SITE_FWD_KV_FULL = 0x103,
+  SITE_FWD_P_FULL = 0x104,
+  SITE_FWD_S_FULL = 0x105,
+  SITE_FWD_O_DONE = 0x106,
+  SITE_FWD_DRAIN = 0x107,
+};
+
+__device__ __forceinline__ bool mask_entry(const FwdParams& p, int row, int col) {
+  return p.block_mask[(size_t)(row / p.mask_bq) * p.n_bc + (col / p.mask_bkv)] != 0;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(FWD_THREADS, 1)
+    ffa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using Cfg = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + Cfg::Q_OFF;
+  uint8_t* sKV = smem + Cfg::KV_OFF;
+  FwdBars* bars = reinterpret_cast<FwdBars*>(smem + Cfg::BAR_OFF);
+  uint16_t* list = reinterpret_cast<uint16_t*>(smem + Cfg::LIST_OFF);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int BH = p.B * p.Hq;
+  const int bid = blockIdx.x;
+  // LPT order: with causal masking the last query blocks carry the most key
+  // tiles, so they are dispatched first; heads vary fastest so that the query
+  // heads of one GQA group (which share K/V) run side by side.
+  const int qblk = p.causal ? (p.n_qblk - 1 - bid / BH) : (bid / BH);
+  const int bh = bid % BH;
+  const int b = bh / p.Hq;
+  const int h = bh % p.Hq;
+  const int hkv = h / (p.Hq / p.Hkv);
+
+  const int q_lo = qblk * (FWD_BM * FWD_NQT);
+  const int q_hi = min(q_lo + FWD_BM * FWD_NQT, p.Sq) - 1;
+  const int a_lo = q_lo + p.q_offset;
+  const int a_hi = q_hi + p.q_offset;
+  const int n_kv = (p.Skv + FWD_BN - 1) / FWD_BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], FWD_BM);
+      mbar_init(&bars->o_done[t], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    for (int i = 0; i < Cfg::NBUF; ++i) {
+      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->kv_empty[i], 1);
+    }
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == FWD_WARP_MMA) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == FWD_WARP_LOAD) {
+    // Key-tile range allowed by causal / window masks, then filtered by the
+    // block mask (a tile stays if any of its (row, col) pairs is kept).
+    int j_hi = n_kv;
+    if (p.causal) j_hi = min(n_kv, a_hi >= 0 ? a_hi / FWD_BN + 1 : 0);
+    int j_lo = 0;
+    if (p.window > 0) {
+      const int lo_col = a_lo - p.window + 1;
+      if (lo_col > 0) j_lo = min(lo_col / FWD_BN, j_hi);
+    }
+    if (p.block_mask == nullptr) {
+      if (lane == 0) {
+        bars->j_lo = j_lo;
+        bars->n_tiles = max(0, j_hi - j_lo);
+        bars->use_list = 0;
+      }
+    } else {
+      int count = 0;
+      const int br_lo = q_lo / p.mask_bq, br_hi = q_hi / p.mask_bq;
+      for (int j0 = j_lo; j0 < j_hi; j0 += 32) {
+        const int j = j0 + lane;
+        bool keep = false;
+        if (j < j_hi) {
+          const int bc_lo = (j * FWD_BN) / p.mask_bkv;
+          const int bc_hi = min(j * FWD_BN + FWD_BN, p.Skv) - 1;
+          for (int br = br_lo; br <= br_hi && !keep; ++br)
+            for (int bc = bc_lo; bc <= bc_hi / p.mask_bkv && !keep; ++bc)
+              keep = p.block_mask[(size_t)br * p.n_bc + bc] != 0;
+        }
+        const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+        const int pos = count + __popc(ballot & ((1u << lane) - 1u));
+        if (keep && pos < FWD_MAX_LIST) list[pos] = (uint16_t)j;
+        count += __popc(ballot);
+      }
+      if (lane == 0) {
+        bars->j_lo = 0;
+        bars->n_tiles = min(count, FWD_MAX_LIST);
+        bars->use_list = 1;
+        if (count > FWD_MAX_LIST && p.ec.err) atomicCAS(p.ec.err, 0u, 0x1FFu);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = bars->tmem_base;
+  const int n = bars->n_tiles;
+  const int j_lo = bars->j_lo;
+  const bool use_list = bars->use_list != 0;
+  auto tile_at = [&](int it) -> int { return use_list ? (int)list[it] : j_lo + it; };
+  constexpr uint32_t FMT = DtypeFmt<T>::value;
+
+  if (warp == FWD_WARP_LOAD) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(&bars->q_full, FWD_NQT * Cfg::TILE);
+      for (int t = 0; t < FWD_NQT; ++t)
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(&tmQ, &bars->q_full, sQ + t * Cfg::TILE + c * (FWD_BM * 128), c * 64, q_lo + t * FWD_BM,
+                      h, b, pol_q);
+      int issued = 0;  // key/value slots armed so far
+      for (int it = 0; it < n; ++it) {
+        const int j = tile_at(it);
+        bool ok = true;
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          const int s = 2 * it + kv;
+          const int buf = s % Cfg::NBUF;
+          const int use = s / Cfg::NBUF;
+          if (use > 0 && !mbar_wait(&bars->kv_empty[buf], (use - 1) & 1, p.ec, abort_flag, SITE_FWD_KV_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->kv_full[buf], Cfg::TILE);
+          ++issued;
+          uint8_t* dst = sKV + buf * Cfg::TILE;
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(kv ? &tmV : &tmK, &bars->kv_full[buf], dst + c * (FWD_BN * 128), c * 64, j * FWD_BN,
+                        hkv, b, pol_kv);
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // Let copies still in flight land before the CTA gives up its smem.
+        mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+        for (int s = max(0, issued - Cfg::NBUF); s < issued; ++s)
+          mbar_wait(&bars->kv_full[s % Cfg::NBUF], (s / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+      }
+    }
+    __syncwarp();
+  } else if (warp == FWD_WARP_MMA) {
+    // ---------------------------- MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc_f16(FWD_BM, FWD_BN, FMT, 0, 0);
+      const uint32_t idesc_pv = make_idesc_f16(FWD_BM, D, FMT, 0, 1);
+      const uint32_t sQa = smem_u32(sQ);
+      const uint32_t sKVa = smem_u32(sKV);
+      auto issue_qk = [&](int t, int buf) {
+        const uint32_t d = tmem + t * 128;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = (ks / 4) * (FWD_BM * 128) + (ks % 4) * 32;
+          const uint64_t a = make_sdesc_sw128(sQa + t * Cfg::TILE + off, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(sKVa + buf * Cfg::TILE + off, 16, 1024);
+          mma_ss(d, a, bd, idesc_qk, ks > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int buf, bool acc) {
+        const uint32_t d = tmem + 256 + t * 128;
+        const uint32_t a = tmem + t * 128;
+#pragma unroll
+        for (int ks = 0; ks < FWD_BN / 16; ++ks) {
+          const uint64_t bd = make_sdesc_sw128(sKVa + buf * Cfg::TILE + ks * 16 * 128, FWD_BN * 128, 1024);
+          mma_ts(d, a + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = n == 0 || mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_Q);
+      if (ok && n > 0) {
+        ok = mbar_wait(&bars->kv_full[0], 0, p.ec, abort_flag, SITE_FWD_KV_FULL);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0, 0);
+          mma_commit(&bars->s_full[0]);
+          issue_qk(1, 0);
+          mma_commit(&bars->s_full[1]);
+          mma_commit(&bars->kv_empty[0]);
+        }
+      }
+      for (int it = 0; it < n && ok; ++it) {
+        const int vs = 2 * it + 1, vb = vs % Cfg::NBUF;
+        const bool has_next = it + 1 < n;
+        const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
+        if (!mbar_wait(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
+        for (int t = 0; t < FWD_NQT && ok; ++t) {
+          if (!mbar_wait(&bars->p_full[t], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, vb, it > 0);
+          mma_commit(&bars->o_done[t]);
+          if (has_next) {
+            if (t == 0 && !mbar_wait(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(t, kb);
+            mma_commit(&bars->s_full[t]);
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bars->kv_empty[vb]);
+        if (has_next) mma_commit(&bars->kv_empty[kb]);
+      }
+      // Every MMA must retire before TMEM is released.
+      mma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ softmax -------------------------------
+    const int t = warp / 4;
+    const int r = threadIdx.x % FWD_BM;
+    const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const int row = q_lo + t * FWD_BM + r;
+    const int arow = row + p.q_offset;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int it = 0; it < n; ++it) {
+      const int j = tile_at(it);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], it & 1, p.ec, abort_flag, SITE_FWD_S_FULL));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[FWD_BN];
+#pragma unroll
+      for (int c = 0; c < FWD_BN; c += 32) tmem_ld32(tS + c, s + c);
+#pragma unroll
+      for (int c = 0; c < FWD_BN; c += 32) tmem_ld_wait32(s + c);
+      float x[FWD_BN];
+      if (p.use_softcap) {
+#pragma unroll
+        for (int c = 0; c < FWD_BN; ++c) x[c] = tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post;
+      } else {
+#pragma unroll
+        for (int c = 0; c < FWD_BN; ++c) x[c] = __uint_as_float(s[c]) * p.scale_log2;
+      }
+      const int c0 = j * FWD_BN;
+      const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) ||
+                             (p.window > 0 && c0 < a_hi - p.window + 1) || (c0 + FWD_BN > p.Skv) ||
+                             (p.block_mask != nullptr);
+      if (need_mask) {
+        const int hi = p.causal ? arow : 0x7fffffff;
+        const int lo = p.window > 0 ? arow - p.window + 1 : -0x7fffffff;
+#pragma unroll
+        for (int c = 0; c < FWD_BN; ++c) {
+          const int col = c0 + c;
+          bool keep = col < p.Skv && col <= hi && col >= lo;
+          if (p.block_mask != nullptr && keep) keep = mask_entry(p, min(row, p.Sq - 1), col);
+          if (!keep) x[c] = -INFINITY;
+        }
+      }
+      float mt = x[0];
+#pragma unroll
+      for (int c = 1; c < FWD_BN; ++c) mt = fmaxf(mt, x[c]);
+      const float m_new = fmaxf(m, mt);
+      const bool resc = m_new > m + RESCALE_LOG2;
+      const bool warp_resc = __any_sync(0xffffffffu, resc);
+      float alpha = 1.f;
+      if (warp_resc) {
+        alpha = (m_new == -INFINITY) ? 1.f : ex2(m - m_new);
+        l *= alpha;
+        m = m_new;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float ls = 0.f;
+      uint32_t pk[FWD_BN / 2];
+#pragma unroll
+      for (int c = 0; c < FWD_BN / 2; ++c) {
+        const float p0 = ex2(x[2 * c] - mu);
+        const float p1 = ex2(x[2 * c + 1] - mu);
+        ls += p0 + p1;
+        pk[c] = pack2<T>(p0, p1);
+      }
+      l += ls;
+      tmem_st32(tS, pk);
+      tmem_st32(tS + 32, pk + 32);
+      // O must carry the new max before this tile's P·V accumulates into it.
+      // P·V of the previous tile retired before this tile's S was produced
+      // (the tensor core runs in issue order), so the wait below is immediate.
+      if (warp_resc && it > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bars->o_done[t], (it - 1) & 1, p.ec, abort_flag, SITE_FWD_O_DONE));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          uint32_t ov[32];
+          tmem_ld32(tO + c, ov);
+          tmem_ld_wait32(ov);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(tO + c, ov);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[t]);
+    }
+    // ------------------------------ epilogue ------------------------------
+    const bool have_o =
+        ok && n > 0 &&
+        __all_sync(0xffffffffu, mbar_wait(&bars->o_done[t], (n - 1) & 1, p.ec, abort_flag, SITE_FWD_O_DONE));
+    if (have_o) tc_fence_after();
+    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)h * p.o_sh + (size_t)row * p.o_ss;
+    const bool store = row < p.Sq;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t ov[32];
+      if (have_o) {
+        tmem_ld32(tO + c, ov);
+        tmem_ld_wait32(ov);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = 0u;
+      }
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        pk[e] = pack2<T>(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
+      if (store) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+      }
+    }
+    if (store && p.lse != nullptr) {
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      const float lse = (l > 0.f) ? (mu + lg2(l)) * 0.6931471805599453f : -INFINITY;
+      p.lse[((size_t)b * p.Hq + h) * p.Sq + row] = lse;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == FWD_WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <typename T, int D>
+static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdParams& p,
+                      int grid, cudaStream_t stream) {
+  using Cfg = FwdCfg<D>;
+  auto kern = ffa_fwd_kernel<T, D>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    if (st) return st;
+    attr_set = true;
+  }
+  kern<<<grid, FWD_THREADS, Cfg::SMEM, stream>>>(mq, mk, mv, p);
+  return launch_status();
+}
+
+}  // namespace ffa
+
+extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B,
+                       int Hq, int Hkv, int Sq, int Skv, int D, const int64_t* q_strides,
+                       const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, float scale,
+                       int causal, int q_offset, int window, float softcap, const uint8_t* block_mask, int n_br,
+                       int n_bc, int mask_bq, int mask_bkv, uint32_t* dev_err, void* stream) {
+  using namespace ffa;
+  if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides) return FFA_ERR_INVALID_ARG;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv < 0 || Hq % Hkv != 0) return FFA_ERR_INVALID_ARG;
+  if (D != 64 && D != 128) return FFA_ERR_UNSUPPORTED;
+  if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
+  if (Skv > 65535 * FWD_BN) return FFA_ERR_UNSUPPORTED;
+  if (block_mask && (n_br <= 0 || n_bc <= 0 || mask_bq <= 0 || mask_bkv <= 0 ||
+                     (int64_t)n_br * mask_bq < Sq || (int64_t)n_bc * mask_bkv < Skv))
+    return FFA_ERR_INVALID_ARG;
+  if (!aligned16(o) || (o_strides[2] % 8) || (o_strides[1] % 8) || (o_strides[0] % 8)) return FFA_ERR_INVALID_ARG;
+
+  FwdParams p{};
+  p.o = o;
+  p.lse = lse;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_ss = o_strides[2];
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.q_offset = q_offset;
+  p.n_qblk = (Sq + FWD_BM * FWD_NQT - 1) / (FWD_BM * FWD_NQT);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.use_softcap = softcap > 0.f;
+  p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
+  p.sc_post = p.use_softcap ? softcap * 1.4426950408889634f : 0.f;
+  p.causal = causal;
+  p.window = window > 0 ? window : 0;
+  p.block_mask = block_mask;
+  p.n_br = n_br;
+  p.n_bc = n_bc;
+  p.mask_bq = mask_bq;
+  p.mask_bkv = mask_bkv;
+  p.ec.err = dev_err;
+  p.ec.limit_ns = wait_limit_ns();
+
+  const CUtensorMapDataType dt =
+      dtype == FFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mq, mk, mv;
+  const int skv_map = Skv > 0 ? Skv : 1;
+  int st = make_tmap_4d(&mq, q, dt, 2, D, Sq, Hq, B, q_strides[2] * 2, q_strides[1] * 2, q_strides[0] * 2, 64,
+                        FWD_BM);
+  if (!st)
+    st = make_tmap_4d(&mk, k, dt, 2, D, skv_map, Hkv, B, k_strides[2] * 2, k_strides[1] * 2, k_strides[0] * 2, 64,
+                      FWD_BN);
+  if (!st)
+    st = make_tmap_4d(&mv, v, dt, 2, D, skv_map, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
+                      FWD_BN);
+  if (st) return st;
+
+  const long long grid = (long long)p.n_qblk * B * Hq;
+  if (grid > 0x7fffffffLL) return FFA_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == FFA_DTYPE_BF16) {
+    if (D == 64) return launch_fwd<__nv_bfloat16, 64>(mq, mk, mv, p, (int)grid, s);
+    return launch_fwd<__nv_bfloat16, 128>(mq, mk, mv, p, (int)grid, s);
+  }
+  if (D == 64) return launch_fwd<__half, 64>(mq, mk, mv, p, (int)grid, s);
+  return launch_fwd<__half, 128>(mq, mk, mv, p, (int)grid, s);
+}

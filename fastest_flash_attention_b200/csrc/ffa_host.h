@@ -1,0 +1,36 @@
+// Host-side plumbing shared by the C-ABI entry points: CUDA error capture,
+// the per-thread wait limit, and TMA tensor-map encoding through the driver
+// entry point (so the library does not link libcuda directly).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ffa_b200.h"
+
+namespace ffa {
+
+void set_last_error(const char* msg);
+unsigned long long wait_limit_ns();
+
+// Records the CUDA error string (if any) and maps it to a status.
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return FFA_OK;
+  set_last_error(cudaGetErrorString(e));
+  return FFA_ERR_CUDA;
+}
+
+// Status of the most recent launch on this thread.
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+
+// Encodes a 4-D tiled TMA map over a row-major tensor whose innermost dim is
+// contiguous: dims {d0 (contiguous), d1, d2, d3}, byte strides for d1..d3,
+// box {b0, b1, 1, 1}, 128-byte swizzle, zero fill out of bounds.
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t d0,
+                 uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1_bytes, uint64_t s2_bytes, uint64_t s3_bytes,
+                 uint32_t b0, uint32_t b1);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace ffa

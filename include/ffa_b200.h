@@ -1,0 +1,85 @@
+/*
+ * ffa_b200.h — C ABI of the B200 (sm_100a) flash-attention kernels.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes,
+ * launches on the given CUDA stream (cudaStream_t passed as void*), never
+ * throws, never allocates device memory, and returns an ffa_status.  Tensors
+ * are row-major in their last dimension (stride 1); the other strides are in
+ * elements.  The library is loaded by the Python package through ctypes and
+ * can be bound the same way from any FFI.
+ *
+ * Reference interfaces replaced (MindIntels/fastest_flash_attention, paths
+ * relative to the project root):
+ *   ffa_fwd            <- ops/attention_forward.py:23  fastest_flash_attn_forward
+ *                         kernels/cpu_reference.py:132 flash_attn_cpu_forward
+ *                         kernels/cpu_fa4.py:219       fa4_forward
+ *                         kernels/triton_fwd.py:144, kernels/triton_ffpa.py:217
+ *   ffa_bwd*           <- ops/attention_backward.py:19 fastest_flash_attn_backward
+ *                         kernels/cpu_reference.py:319 flash_attn_cpu_backward
+ *                         kernels/cpu_fa4.py:445       fa4_backward
+ *                         kernels/triton_bwd.py:122
+ *   ffa_paged_*        <- ops/kv_cache.py:170 PagedKVCache.append_tokens and
+ *                         ops/kv_cache.py:208 get_kv + the forward it feeds
+ *   ffa_mla_*          <- modules/flash_mla.py:116 FastestFlashMLA.forward
+ *                         (absorbed latent form of the same attention)
+ */
+#ifndef FFA_B200_H_
+#define FFA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FFA_OK = 0,
+  FFA_ERR_INVALID_ARG = 1,     /* bad shape / stride / alignment / pointer */
+  FFA_ERR_UNSUPPORTED = 2,     /* valid request outside what the kernels cover */
+  FFA_ERR_CUDA = 3,            /* a CUDA runtime/driver call failed */
+  FFA_ERR_DEVICE_TIMEOUT = 4,  /* a bounded in-kernel wait expired (see ffa_read_error) */
+  FFA_ERR_WORKSPACE = 5        /* workspace missing or too small */
+} ffa_status;
+
+typedef enum { FFA_DTYPE_F16 = 0, FFA_DTYPE_BF16 = 1 } ffa_dtype;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ffa_version(void);
+
+/* Last CUDA error string seen by the library on this thread (static storage). */
+const char* ffa_last_error(void);
+
+/* Device error word helpers: kernels record the site code of an expired wait
+ * into a caller-provided uint32 in device memory (nullptr disables it).
+ * ffa_read_error copies it to *out (synchronising `stream`). */
+int ffa_read_error(const uint32_t* dev_err, uint32_t* out, void* stream);
+
+/* Wall-clock limit (nanoseconds) applied to every in-kernel wait of later
+ * launches on this host thread; default 2e9 (2 s). */
+void ffa_set_wait_limit_ns(unsigned long long ns);
+
+/* ----------------------------------------------------------------------------
+ * Prefill / training forward.
+ *   q  [B, Hq,  Sq,  D ]   k [B, Hkv, Skv, D]   v [B, Hkv, Skv, D]
+ *   o  [B, Hq,  Sq,  D ]   lse [B, Hq, Sq] fp32 (natural log), may be NULL
+ * Strides are given as {batch, head, seq} in elements for each tensor.
+ * GQA/MQA: Hq % Hkv == 0, query head h reads kv head h / (Hq / Hkv).
+ * causal: key j is visible to query i iff j <= i + q_offset.
+ * window > 0: key j visible iff j >= i + q_offset - window + 1.
+ * softcap > 0: scores become softcap * tanh(score * scale / softcap).
+ * block_mask (uint8 [n_br, n_bc], 1 = keep) masks every (query, key) pair whose
+ *   (i / mask_bq, j / mask_bkv) entry is 0; NULL disables it.
+ * Supported: D in {64, 128}, dtype f16/bf16.
+ * ------------------------------------------------------------------------- */
+int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B, int Hq,
+            int Hkv, int Sq, int Skv, int D, const int64_t* q_strides, const int64_t* k_strides,
+            const int64_t* v_strides, const int64_t* o_strides, float scale, int causal, int q_offset,
+            int window, float softcap, const uint8_t* block_mask, int n_br, int n_bc, int mask_bq,
+            int mask_bkv, uint32_t* dev_err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFA_B200_H_ */
