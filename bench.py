@@ -1,0 +1,352 @@
+"""Benchmark of the attention hot path on B200.
+
+Default workload (the configuration the headline metric is quoted on): GQA
+prefill forward, bf16, B=4, Hq=32, Hkv=8, S=8192, D=128, causal, emitting O
+and LSE.  A step = one forward over one batch of synthetic inputs (~N(0,1)
+scaled by D^-1/4, seeded); inputs (403 MB) exceed the 126 MB L2, so no flush
+is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs one process per GPU (torchrun); every rank processes its own full
+batch (weak scaling, no collective on the data path) and rank 0 prints the
+whole-job aggregate over the max-over-ranks time.
+
+--impl reference times the reference's CPU algorithm (the numpy port in
+oracle/, the reference being a Python package that cannot travel) on the
+host cores, on a bounded sample of the same workload, and reports the same
+metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "causal attention fwd TFLOP/s (GQA prefill bf16, B=4 Hq=32 Hkv=8 S=8192 D=128)"
+UNIT = "TFLOP/s"
+CFG = dict(B=4, Hq=32, Hkv=8, S=8192, D=128)
+# --case small: same kernel, half the batch (192 MB of inputs, still above L2) for ncu captures
+SMALL_CFG = dict(B=2, Hq=32, Hkv=8, S=8192, D=128)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def causal_pairs(S: int) -> int:
+    return S * (S + 1) // 2
+
+
+def fwd_flops(B, Hq, S, D) -> float:
+    # 2 GEMMs (QK^T and PV) of 2*D flops per unmasked (query, key) pair
+    return 4.0 * D * causal_pairs(S) * B * Hq
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "GQA causal prefill forward (O + LSE)",
+        "batch_per_gpu": CFG["B"], "q_heads": CFG["Hq"], "kv_heads": CFG["Hkv"], "seq_len": CFG["S"],
+        "head_dim": CFG["D"], "causal": True, "parallelism": f"shard-by-batch x{n_gpus} (no collective)",
+        "l2": "inputs 403 MB per GPU > 126 MB L2, no flush needed",
+        "flop_convention": "4*D*causal_pairs*B*Hq (exact unmasked pairs)",
+    }
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend)
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(device, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    sc = D ** -0.25
+    q = (torch.randn(B, Hq, S, D, generator=g) * sc).to(torch.bfloat16)
+    k = (torch.randn(B, Hkv, S, D, generator=g) * sc).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+# ----------------------------------------------------------------------------
+# CPU arm: the reference algorithm (numpy port) on a bounded sample
+# ----------------------------------------------------------------------------
+
+def cpu_reference_sample(q, k, v, heads: int = 4, s_len: int = 8192, block: int = 128):
+    """Time the oracle forward on `heads` query heads of batch 0 with the
+    first `s_len` positions (causal), returning (TFLOP/s, seconds, sample)."""
+    from oracle import attention_oracle as O
+    D = q.shape[-1]
+    g = CFG["Hq"] // CFG["Hkv"]
+    qs = q[:1, :heads, :s_len].float().numpy()
+    ks = np.repeat(k[:1, :max(1, heads // g), :s_len].float().numpy(), g, axis=1)[:, :heads]
+    vs = np.repeat(v[:1, :max(1, heads // g), :s_len].float().numpy(), g, axis=1)[:, :heads]
+    t0 = time.perf_counter()
+    O.flash_forward(qs, ks, vs, scale=1.0 / math.sqrt(D), causal=True, block_q=block, block_kv=block,
+                    return_lse=True)
+    dt = time.perf_counter() - t0
+    fl = fwd_flops(1, heads, s_len, D)
+    sample = f"batch 0, {heads} query head(s), first {s_len} positions, causal, block {block} (numpy fp32)"
+    return fl / dt / 1e12, dt, sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    q, k, v = make_inputs("cpu")
+    cores = os.cpu_count() or 1
+    vals = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        tf, dt, sample = cpu_reference_sample(q, k, v)
+        if i >= args.warmup:
+            vals.append(tf)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)*D^-1/4, bf16-rounded)",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def run_ours(args, world, rank, local):
+    from fastest_flash_attention_b200 import fastest_flash_attn_forward
+    from fastest_flash_attention_b200.attention import flash_fwd
+    from fastest_flash_attention_b200 import _lib
+
+    dev = torch.device("cuda", local)
+    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    scale = 1.0 / math.sqrt(D)
+    q_h, k_h, v_h = make_inputs("cpu", seed=rank)
+    q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
+    flops = fwd_flops(B, Hq, S, D)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- device-resident timing (value + roofline) ----
+    for _ in range(args.warmup):
+        flash_fwd(q, k, v, scale=scale, causal=True)
+    torch.cuda.synchronize(dev)
+    _lib.check_device_errors(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            flash_fwd(q, k, v, scale=scale, causal=True)
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    _lib.check_device_errors(dev)
+    ms_local = t0.elapsed_time(t1) / args.steps
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    ms = max_over_ranks(ms_local, world)
+    value = world * flops / (ms * 1e-3) / 1e12
+
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "ms_per_step": ms,
+                              "config": workload_config(world), "note": "kernel-only run (--kernel-only)"}))
+        return
+
+    # ---- end to end through the public API with host buffers ----
+    qp, kp, vp = q_h.pin_memory(), k_h.pin_memory(), v_h.pin_memory()
+    o_host = torch.empty(q_h.shape, dtype=torch.bfloat16).pin_memory()
+    lse_host = torch.empty((B, Hq, S, 1), dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (qp, kp, vp))
+    d2h = o_host.numel() * 2 + lse_host.numel() * 4
+
+    def e2e_step():
+        qd = qp.to(dev, non_blocking=True)
+        kd = kp.to(dev, non_blocking=True)
+        vd = vp.to(dev, non_blocking=True)
+        o, lse = fastest_flash_attn_forward(qd, kd, vd, causal=True, return_lse=True)
+        o_host.copy_(o, non_blocking=True)
+        lse_host.copy_(lse, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    e2e_val = world * flops / (e2e_ms * 1e-3) / 1e12
+    _lib.check_device_errors(dev)
+
+    if rank != 0:
+        return
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    achieved = flops / (launch_ms * 1e-3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "fwd_gqa_prefill_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*D^-1/4)",
+        "config": workload_config(world),
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "api": "fastest_flash_attn_forward(causal=True, return_lse=True)"},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_src} bf16_tflops (burst)", "kernel": "ffa_fwd_kernel<bf16,128>",
+                     "algorithmic_flops_per_launch": flops},
+        "clocks": clk.summary(),
+    }
+    if world == 1:
+        runs = [cpu_reference_sample(q_h, k_h, v_h) for _ in range(3)]
+        tfc = statistics.median(r[0] for r in runs)
+        line["cpu_baseline"] = {"value": tfc, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": runs[0][2] + ", median of 3",
+                                "seconds": sum(r[1] for r in runs)}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--case", choices=["full", "small"], default="full")
+    ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
+    args = ap.parse_args()
+    if args.case == "small":
+        CFG.update(SMALL_CFG)
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_init()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -3,5 +3,11 @@ MindIntels/fastest_flash_attention (reference __init__.py:40-88)."""
 from .config import AttentionConfig
 from .utils import auto_select_block_size, check_triton_available
 from .attention import fastest_flash_attn_forward
+from .block_sparse import (
+    create_causal_block_mask,
+    create_sliding_window_block_mask,
+    create_local_block_mask,
+    combine_block_masks,
+)
 
 __version__ = "1.0.0"
