@@ -87,13 +87,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
                                           volatile int* abort, uint32_t site, bool drain = false) {
   if (mbar_test(bar, parity)) return true;
   if (!drain && *abort) return false;
-  unsigned long long t0 = global_ns();
+  // The limit is counted in SM clock cycles (cheap to read); 2 cycles per ns
+  // over-approximates every B200 clock, so the wall-clock bound still holds.
+  const long long t0 = clock64();
+  const long long limit = (long long)(ec.limit_ns * 2ull);
   uint32_t spins = 0;
   while (true) {
     if (mbar_test(bar, parity)) return true;
-    if (((++spins) & 63u) == 0) {
+    if (((++spins) & 15u) == 0) {
       if (!drain && *abort) return false;
-      if (global_ns() - t0 > ec.limit_ns) {
+      if (clock64() - t0 > limit) {
         *abort = 1;
         if (ec.err) atomicCAS(ec.err, 0u, site);
         return false;
@@ -258,6 +261,18 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Re-balance the register file between warpgroups (all warps of a
+// warpgroup execute the same call).  The per-warpgroup budgets of a kernel
+// must add up to at most its launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------ math ---------------------------------------
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -279,6 +294,55 @@ __device__ __forceinline__ float rcp(float x) {
 __device__ __forceinline__ float tanh_acc(float x) {
   const float e = ex2(x * 2.8853900817779268f);  // 2*log2(e)
   return 1.0f - 2.0f * rcp(e + 1.0f);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed fp32x2 arithmetic (one FMA-pipe instruction for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x on the FMA pipe, for two lanes at once, to offload the MUFU unit.
+// x = n + f with n = rint(x) (magic-constant rounding), f in [-1/2, 1/2];
+// 2^f by a cubic whose coefficients are the relative-error minimax fit from
+// csrc/fit_exp2_poly.py (Remez exchange; max relative error 7.5e-5); 2^n is
+// applied by adding n to the exponent field.  Inputs below -126 return 0.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  // Below -126 the result would be a denormal: flush to 0 like ex2.approx.ftz
+  // (and keep -inf -> exactly 0, which masked scores rely on).
+  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const float2 t = fadd2(xc, magic);                       // low mantissa bits hold rint(x)
+  const float2 n = fadd2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = ffma2(n, make_float2(-1.f, -1.f), xc);  // x - n in [-1/2, 1/2]
+  float2 p = make_float2(5.517166853e-02f, 5.517166853e-02f);
+  p = ffma2(p, f, make_float2(2.426111251e-01f, 2.426111251e-01f));
+  p = ffma2(p, f, make_float2(6.932609677e-01f, 6.932609677e-01f));
+  p = ffma2(p, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
+  float2 r;
+  r.x = x.x < -126.f ? 0.f : __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  r.y = x.y < -126.f ? 0.f : __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return r;
 }
 
 template <typename T>

@@ -27,11 +27,15 @@ namespace ffa {
 constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
 constexpr int FWD_NQT = 2;    // query tiles per CTA
 constexpr int FWD_BN = 128;   // keys per key tile
-constexpr int FWD_THREADS = 320;
+constexpr int FWD_THREADS = 384;  // 2 softmax warpgroups + 1 warpgroup for TMA / MMA (2 warps idle)
+// Register budgets after the split: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
+constexpr uint32_t FWD_REGS_SOFTMAX = 208;
+constexpr uint32_t FWD_REGS_OTHER = 88;
 constexpr int FWD_WARP_LOAD = 8;
 constexpr int FWD_WARP_MMA = 9;
 constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block mask filters them
 constexpr float RESCALE_LOG2 = 8.0f;
+constexpr int FWD_PCH = 4;  // P is handed to the MMA warp in 4 chunks of 32 keys
 
 template <int D>
 struct FwdCfg {
@@ -63,7 +67,7 @@ struct FwdParams {
 struct FwdBars {
   uint64_t q_full;
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_full[2][FWD_PCH];
   uint64_t o_done[2];
   uint64_t drain;
   uint64_t kv_full[8];
@@ -125,7 +129,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     mbar_init(&bars->q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], FWD_BM);
+      for (int k = 0; k < FWD_PCH; ++k) mbar_init(&bars->p_full[t][k], FWD_BM);
       mbar_init(&bars->o_done[t], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -193,7 +197,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   auto tile_at = [&](int it) -> int { return use_list ? (int)list[it] : j_lo + it; };
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (warp == FWD_WARP_LOAD) {
+  if (warp >= 8) {
+   regs_dec<FWD_REGS_OTHER>();
+   if (warp == FWD_WARP_LOAD) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -240,25 +246,33 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = make_idesc_f16(FWD_BM, FWD_BN, FMT, 0, 0);
       const uint32_t idesc_pv = make_idesc_f16(FWD_BM, D, FMT, 0, 1);
-      const uint32_t sQa = smem_u32(sQ);
-      const uint32_t sKVa = smem_u32(sKV);
+      // Descriptors are built once; every MMA then only adds a constant
+      // (address >> 4) offset to the low bits, keeping this single issuing
+      // thread's instruction count (and so its issue-slot needs) minimal.
+      const uint64_t q_base = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_base = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
+      const uint64_t v_base = make_sdesc_sw128(smem_u32(sKV), FWD_BN * 128, 1024);
       auto issue_qk = [&](int t, int buf) {
         const uint32_t d = tmem + t * 128;
+        const uint64_t qa = q_base + (uint64_t)((t * Cfg::TILE) >> 4);
+        const uint64_t kb = k_base + (uint64_t)((buf * Cfg::TILE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = (ks / 4) * (FWD_BM * 128) + (ks % 4) * 32;
-          const uint64_t a = make_sdesc_sw128(sQa + t * Cfg::TILE + off, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(sKVa + buf * Cfg::TILE + off, 16, 1024);
-          mma_ss(d, a, bd, idesc_qk, ks > 0);
+          const uint32_t off = ((ks / 4) * (FWD_BM * 128) + (ks % 4) * 32) >> 4;
+          mma_ss(d, qa + off, kb + off, idesc_qk, ks > 0);
         }
       };
-      auto issue_pv = [&](int t, int buf, bool acc) {
+      // P·V for one chunk of keys (k-steps of 16 keys); chunks are issued as
+      // the softmax group releases them.
+      auto issue_pv = [&](int t, int buf, bool acc, int chunk) {
         const uint32_t d = tmem + 256 + t * 128;
         const uint32_t a = tmem + t * 128;
+        const uint64_t vb = v_base + (uint64_t)((buf * Cfg::TILE) >> 4);
+        constexpr int KS_PER = FWD_BN / 16 / FWD_PCH;
 #pragma unroll
-        for (int ks = 0; ks < FWD_BN / 16; ++ks) {
-          const uint64_t bd = make_sdesc_sw128(sKVa + buf * Cfg::TILE + ks * 16 * 128, FWD_BN * 128, 1024);
-          mma_ts(d, a + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        for (int kk = 0; kk < KS_PER; ++kk) {
+          const int ks = chunk * KS_PER + kk;
+          mma_ts(d, a + ks * 8, vb + (uint64_t)((ks * 16 * 128) >> 4), idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
       };
       bool ok = n == 0 || mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_Q);
@@ -279,12 +293,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
         if (!mbar_wait(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
         for (int t = 0; t < FWD_NQT && ok; ++t) {
-          if (!mbar_wait(&bars->p_full[t], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
-            ok = false;
-            break;
+          for (int k = 0; k < FWD_PCH; ++k) {
+            if (!mbar_wait(&bars->p_full[t][k], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, vb, it > 0, k);
           }
-          tc_fence_after();
-          issue_pv(t, vb, it > 0);
+          if (!ok) break;
           mma_commit(&bars->o_done[t]);
           if (has_next) {
             if (t == 0 && !mbar_wait(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
@@ -305,7 +322,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       mbar_wait(&bars->drain, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
     }
     __syncwarp();
+   }
   } else {
+    regs_inc<FWD_REGS_SOFTMAX>();
     // ------------------------------ softmax -------------------------------
     const int t = warp / 4;
     const int r = threadIdx.x % FWD_BM;
@@ -326,13 +345,14 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       for (int c = 0; c < FWD_BN; c += 32) tmem_ld32(tS + c, s + c);
 #pragma unroll
       for (int c = 0; c < FWD_BN; c += 32) tmem_ld_wait32(s + c);
-      float x[FWD_BN];
+      // Scores in base-2 units are  s * mul  (mul = scale*log2 e), or, with a
+      // softcap, softcap*tanh(s*scale/softcap)*log2 e computed in place (mul = 1).
+      float mul = p.scale_log2;
       if (p.use_softcap) {
 #pragma unroll
-        for (int c = 0; c < FWD_BN; ++c) x[c] = tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post;
-      } else {
-#pragma unroll
-        for (int c = 0; c < FWD_BN; ++c) x[c] = __uint_as_float(s[c]) * p.scale_log2;
+        for (int c = 0; c < FWD_BN; ++c)
+          s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+        mul = 1.f;
       }
       const int c0 = j * FWD_BN;
       const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) ||
@@ -346,34 +366,26 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           const int col = c0 + c;
           bool keep = col < p.Skv && col <= hi && col >= lo;
           if (p.block_mask != nullptr && keep) keep = mask_entry(p, min(row, p.Sq - 1), col);
-          if (!keep) x[c] = -INFINITY;
+          if (!keep) s[c] = __float_as_uint(-INFINITY);
         }
       }
-      float mt = x[0];
+      // Row max: eight independent 3-input max chains, then a small tree.
+      float mx[8];
 #pragma unroll
-      for (int c = 1; c < FWD_BN; ++c) mt = fmaxf(mt, x[c]);
-      const float m_new = fmaxf(m, mt);
-      const bool resc = m_new > m + RESCALE_LOG2;
-      const bool warp_resc = __any_sync(0xffffffffu, resc);
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[i]);
+#pragma unroll
+      for (int c = 8; c < FWD_BN; c += 16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
+      const float mraw = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float m_new = fmaxf(m, mraw * mul);
+      const bool warp_resc = __any_sync(0xffffffffu, m_new > m + RESCALE_LOG2);
       float alpha = 1.f;
       if (warp_resc) {
         alpha = (m_new == -INFINITY) ? 1.f : ex2(m - m_new);
         l *= alpha;
         m = m_new;
       }
-      const float mu = (m == -INFINITY) ? 0.f : m;
-      float ls = 0.f;
-      uint32_t pk[FWD_BN / 2];
-#pragma unroll
-      for (int c = 0; c < FWD_BN / 2; ++c) {
-        const float p0 = ex2(x[2 * c] - mu);
-        const float p1 = ex2(x[2 * c + 1] - mu);
-        ls += p0 + p1;
-        pk[c] = pack2<T>(p0, p1);
-      }
-      l += ls;
-      tmem_st32(tS, pk);
-      tmem_st32(tS + 32, pk + 32);
       // O must carry the new max before this tile's P·V accumulates into it.
       // P·V of the previous tile retired before this tile's S was produced
       // (the tensor core runs in issue order), so the wait below is immediate.
@@ -392,9 +404,36 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           tmem_st32(tO + c, ov);
         }
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->p_full[t]);
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      const float2 mul2 = make_float2(mul, mul);
+      const float2 nmu2 = make_float2(-mu, -mu);
+      // p = 2^(s*mul - mu), written over S as 16-bit pairs one 32-key chunk at
+      // a time; each chunk is released to the MMA warp as soon as it is in
+      // TMEM so P·V overlaps the rest of the exponentials.
+      float2 acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < FWD_PCH; ++k) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int c = k * 16 + e;
+          const float2 a =
+              ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), mul2, nmu2);
+          float2 pv;
+          pv.x = ex2(a.x);
+          pv.y = ex2(a.y);
+          acc[e & 3] = fadd2(acc[e & 3], pv);
+          pk[e] = pack2<T>(pv.x, pv.y);
+        }
+        tmem_st16(tS + k * 16, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[t][k]);
+      }
+      const float2 acct = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+      l += acct.x + acct.y;
     }
     // ------------------------------ epilogue ------------------------------
     const bool have_o =
