@@ -2,7 +2,12 @@
 MindIntels/fastest_flash_attention (reference __init__.py:40-88)."""
 from .config import AttentionConfig
 from .utils import auto_select_block_size, check_triton_available
-from .attention import fastest_flash_attn_forward
+from .attention import (
+    fastest_flash_attn_forward,
+    fastest_flash_attn_backward,
+    fastest_flash_attn_func,
+    FastestFlashAttnFunc,
+)
 from .block_sparse import (
     create_causal_block_mask,
     create_sliding_window_block_mask,

@@ -168,3 +168,119 @@ def fastest_flash_attn_forward(
         if lse is not None:
             lse = lse.squeeze(1)
     return o, lse
+
+
+def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+              lse: torch.Tensor, *, scale: float, causal: bool = False, q_offset: int = 0,
+              window: Optional[int] = None, softcap: Optional[float] = None,
+              compute_dtype: Optional[torch.dtype] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Run the deterministic sm_100a backward on 4-D tensors.
+
+    lse: [B, Hq, Sq] (or [B, Hq, Sq, 1]) natural-log LSE from the forward.
+    Returns (dq, dk, dv) in the kernel dtype; dk/dv have k's head count
+    (GQA groups are summed inside the kernel).
+    """
+    _lib.require_cuda(dout, q, k, v, o, lse)
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    if D not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim {D} not supported by the sm_100a backward kernel")
+    if Hq % Hkv != 0:
+        raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
+    dt = kernel_dtype(q, compute_dtype)
+    q, k, v, o, dout = (_tma_ready(t, dt) for t in (q, k, v, o, dout))
+    if lse.dim() == 4:
+        lse = lse[..., 0]
+    lse = lse.to(torch.float32).contiguous()
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    lib = _lib.load()
+    ws_bytes = lib.ffa_bwd_workspace_size(B, Hq, Sq)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        st = lib.ffa_bwd(
+            dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D,
+            _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o), _strides_bhs(dout),
+            _strides_bhs(dq), _strides_bhs(dk), _strides_bhs(dv),
+            float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),
+            ws.data_ptr(), ws_bytes, _lib.err_word(q.device).data_ptr(), _lib.stream_of(q))
+    _lib.check(st, "ffa_bwd")
+    if _lib.sync_check_enabled():
+        _lib.check_device_errors(q.device)
+    return dq, dk, dv
+
+
+def fastest_flash_attn_backward(
+    grad_output: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    lse: torch.Tensor,
+    *,
+    scale: Optional[float] = None,
+    causal: bool = False,
+    block_size: int = 64,
+    softcap: Optional[float] = None,
+    sliding_window: Optional[int] = None,
+    q_offset: int = 0,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward (ops/attention_backward.py:19-76): (dq, dk, dv) from the
+    forward's output and LSE, recomputing the attention tile by tile.
+
+    ``block_size`` is accepted for compatibility (tiles are fixed at 128).
+    Gradients come back in the dtypes of q, k and v.
+    """
+    dq, dk, dv = flash_bwd(grad_output, q, k, v, output, lse, scale=scale if scale is not None else
+                           1.0 / math.sqrt(q.shape[-1]), causal=causal, q_offset=q_offset, window=sliding_window,
+                           softcap=softcap)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+class FastestFlashAttnFunc(Function):
+    """Autograd function (ops/attention_func.py:20-90): saves q, k, v, output
+    and LSE; the backward recomputes attention with the sm_100a kernels.
+    Accepts GQA (fewer K/V heads than query heads) natively."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass):
+        output, lse = fastest_flash_attn_forward(
+            q, k, v, scale=scale, causal=causal, block_size=block_size, softcap=softcap,
+            sliding_window=sliding_window, two_pass=two_pass, return_lse=True)
+        ctx.save_for_backward(q, k, v, output, lse)
+        ctx.scale = scale
+        ctx.causal = causal
+        ctx.block_size = block_size
+        ctx.softcap = softcap
+        ctx.sliding_window = sliding_window
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, output, lse = ctx.saved_tensors
+        was_3d = q.dim() == 3
+        if was_3d:
+            q, k, v, output, lse, grad_output = (t.unsqueeze(1) for t in (q, k, v, output, lse, grad_output))
+        dq, dk, dv = fastest_flash_attn_backward(
+            grad_output, q, k, v, output, lse, scale=ctx.scale, causal=ctx.causal, block_size=ctx.block_size,
+            softcap=ctx.softcap, sliding_window=ctx.sliding_window)
+        if was_3d:
+            dq, dk, dv = dq.squeeze(1), dk.squeeze(1), dv.squeeze(1)
+        return dq, dk, dv, None, None, None, None, None, None
+
+
+def fastest_flash_attn_func(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: Optional[float] = None,
+    causal: bool = False,
+    block_size: int = 64,
+    softcap: Optional[float] = None,
+    sliding_window: Optional[int] = None,
+    two_pass: bool = False,
+) -> torch.Tensor:
+    """Differentiable attention (ops/attention_func.py:93-125)."""
+    return FastestFlashAttnFunc.apply(q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass)

@@ -1,4 +1,5 @@
 // Host plumbing implementation and the small library-wide C-ABI functions.
+#include <stdio.h>
 #include <string.h>
 
 #include "ffa_host.h"
@@ -34,6 +35,10 @@ static EncodeTiledFn encode_fn() {
 int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t d0,
                  uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1_bytes, uint64_t s2_bytes, uint64_t s3_bytes,
                  uint32_t b0, uint32_t b1) {
+  // The driver-level encode needs the device's primary context current on
+  // this thread (host threads such as autograd workers may not have it yet).
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_last_error("cuTensorMapEncodeTiled entry point unavailable");
@@ -55,7 +60,13 @@ int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_last_error("cuTensorMapEncodeTiled failed");
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu,%llu} byte strides {%llu,%llu,%llu} base %p",
+             (int)r, (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2,
+             (unsigned long long)d3, (unsigned long long)s1_bytes, (unsigned long long)s2_bytes,
+             (unsigned long long)s3_bytes, base);
+    set_last_error(msg);
     return FFA_ERR_INVALID_ARG;
   }
   return FFA_OK;

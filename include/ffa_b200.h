@@ -78,6 +78,27 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
             int window, float softcap, const uint8_t* block_mask, int n_br, int n_bc, int mask_bq,
             int mask_bkv, uint32_t* dev_err, void* stream);
 
+/* ----------------------------------------------------------------------------
+ * Backward (deterministic: fixed summation order, no atomics; bit-identical
+ * results run to run).  Replaces ops/attention_backward.py:19
+ * fastest_flash_attn_backward -> kernels/cpu_reference.py:319 and
+ * kernels/cpu_fa4.py:445.
+ *   dout, o [B, Hq, Sq, D]; lse [B, Hq, Sq] fp32 (natural log, from ffa_fwd)
+ *   dq [B, Hq, Sq, D]; dk, dv [B, Hkv, Skv, D] (GQA groups summed in order)
+ * Same mask / softcap semantics as ffa_fwd (no block mask: the reference
+ * backward has none).  `workspace` must hold ffa_bwd_workspace_size() bytes
+ * of device memory (padded base-2 LSE and Delta = rowsum(dO*O)).
+ * Three kernel launches on `stream`: preprocess, dK/dV, dQ.
+ * ------------------------------------------------------------------------- */
+size_t ffa_bwd_workspace_size(int B, int Hq, int Sq);
+
+int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+            void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq, int Skv, int D,
+            const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+            const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+            const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
+            int window, float softcap, void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
