@@ -16,3 +16,5 @@ from .block_sparse import (
 )
 
 __version__ = "1.0.0"
+from .kv_cache import PagedKVCache, ContinuousKVCache
+from .decode import paged_decode

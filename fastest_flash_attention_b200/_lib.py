@@ -62,6 +62,20 @@ SIGNATURES: dict[str, tuple] = {
         _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
     ]),
+    "ffa_paged_decode_workspace_size": (_c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int]),
+    "ffa_paged_decode": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # q k_pages v_pages block_table ctx_lens
+        _c_void_p, _c_void_p,  # out lse
+        _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype R Hq Hkv D
+        _c_int, _c_int, _c_int,  # num_pages page_size max_pages_per_req
+        _c_i64p, _c_i64p, _c_float, _c_float, _c_int,  # q_strides o_strides scale softcap chunks_per_split
+        _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
+    ]),
+    "ffa_paged_append": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # k_new v_new k_pages v_pages slots
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype n_tokens Hkv D page_size num_pages
+        _c_i64p, _c_void_p,  # new_strides stream
+    ]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -99,6 +99,42 @@ int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const
             const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
             int window, float softcap, void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
+/* ----------------------------------------------------------------------------
+ * Paged-KV decode (one query token per request), split over the context and
+ * merged by LSE.  Replaces ops/kv_cache.py:208 PagedKVCache.get_kv (page
+ * gather) followed by ops/attention_forward.py:23 on the gathered K/V.
+ *   q [R, Hq, D] (strides {request, head} in elements)
+ *   k_pages, v_pages [num_pages, Hkv, page_size, D] contiguous (the
+ *     reference's page pool layout, ops/kv_cache.py:142-149)
+ *   block_table [R, max_pages_per_req] int32 page ids; ctx_lens [R] int32
+ *   out [R, Hq, D] (strides {request, head}); lse [R, Hq] fp32 natural log
+ *     (may be NULL)
+ * page_size must be a multiple of 16; Hq / Hkv <= 16; D in {64, 128}.
+ * chunks_per_split (16-token chunks per CTA; <= 0 selects 32) sets the split
+ * size; `workspace` must hold ffa_paged_decode_workspace_size() bytes.
+ * Two launches on `stream`: split kernel and merge kernel.
+ * ------------------------------------------------------------------------- */
+size_t ffa_paged_decode_workspace_size(int R, int Hq, int D, int max_pages_per_req, int page_size,
+                                       int chunks_per_split);
+
+int ffa_paged_decode(const void* q, const void* k_pages, const void* v_pages, const int* block_table,
+                     const int* ctx_lens, void* out, float* lse, int dtype, int R, int Hq, int Hkv, int D,
+                     int num_pages, int page_size, int max_pages_per_req, const int64_t* q_strides,
+                     const int64_t* o_strides, float scale, float softcap, int chunks_per_split, void* workspace,
+                     size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Paged-KV append: scatter new K/V tokens into their (page, offset) slots.
+ * Replaces the per-token loop of ops/kv_cache.py:170-206
+ * PagedKVCache.append_tokens (slot assignment stays on the host, where the
+ * reference's FIFO page allocator lives).
+ *   k_new, v_new [Hkv, n_tokens, D] (strides {head, token} in elements)
+ *   slots [n_tokens] int32 = page * page_size + offset
+ * ------------------------------------------------------------------------- */
+int ffa_paged_append(const void* k_new, const void* v_new, void* k_pages, void* v_pages, const int* slots,
+                     int dtype, int n_tokens, int Hkv, int D, int page_size, int num_pages,
+                     const int64_t* new_strides, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
