@@ -62,6 +62,14 @@ SIGNATURES: dict[str, tuple] = {
         _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
     ]),
+    "ffa_bwd_noalloc": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # dout q k v o lse
+        _c_void_p, _c_void_p, _c_void_p,  # dq dk dv
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D
+        _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p,  # strides q k v o do dq dk dv
+        _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
+        _c_u32p, _c_void_p,  # err stream
+    ]),
     "ffa_paged_decode_workspace_size": (_c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int]),
     "ffa_paged_decode": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # q k_pages v_pages block_table ctx_lens

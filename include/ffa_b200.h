@@ -100,6 +100,28 @@ int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const
             int window, float softcap, void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Allocation-free backward.  No counterpart in the reference: this entry
+ * point exists for callers that cannot allocate device memory (code handed
+ * only its input/output buffers by a host framework, or hosts that forbid a
+ * device-synchronising cudaMalloc in the middle of a step).  Same arguments
+ * and results as ffa_bwd without the workspace: the scratch rows live in an
+ * array compiled into the library (8 MiB + 256 B held by every GPU that loads
+ * it, until process exit).  Limit: B * Hq * round_up(Sq, 128) <=
+ * FFA_BWD_NOALLOC_MAX_ROWS, else FFA_ERR_UNSUPPORTED.  All calls on a device
+ * share the array, so calls whose kernels overlap on the GPU race.  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture.
+ * ------------------------------------------------------------------------- */
+#define FFA_BWD_NOALLOC_MAX_ROWS (1 << 20)
+
+int ffa_bwd_noalloc(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                    const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq,
+                    int Skv, int D, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                    const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+                    const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
+                    int window, float softcap, uint32_t* dev_err, void* stream);
+
+/* ----------------------------------------------------------------------------
  * Paged-KV decode (one query token per request), split over the context and
  * merged by LSE.  Replaces ops/kv_cache.py:208 PagedKVCache.get_kv (page
  * gather) followed by ops/attention_forward.py:23 on the gathered K/V.
