@@ -18,3 +18,15 @@ from .block_sparse import (
 __version__ = "1.0.0"
 from .kv_cache import PagedKVCache, ContinuousKVCache
 from .decode import paged_decode
+from .fa4 import FA4AttnFunc, fa4_attn_func, fa4_forward_dispatch
+from .modules import FastestFlashMHA, FastestFlashGQA, FastestFlashMLA, FastestFlashFA4, RotaryEmbedding
+from .mla import MLADecoder, MLALatentCache, mla_decode, absorbed_weights
+from .utils import repeat_kv
+
+__all__ = [
+    "AttentionConfig", "fastest_flash_attn_forward", "fastest_flash_attn_backward", "fastest_flash_attn_func",
+    "FastestFlashAttnFunc", "fa4_attn_func", "fa4_forward_dispatch", "FA4AttnFunc", "FastestFlashMHA",
+    "FastestFlashGQA", "FastestFlashMLA", "FastestFlashFA4", "PagedKVCache", "ContinuousKVCache",
+    "create_causal_block_mask", "create_sliding_window_block_mask", "create_local_block_mask",
+    "auto_select_block_size", "check_triton_available", "paged_decode", "MLADecoder", "mla_decode",
+]

@@ -47,7 +47,7 @@ SIGNATURES: dict[str, tuple] = {
     "ffa_set_wait_limit_ns": (None, [ctypes.c_ulonglong]),
     "ffa_fwd": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # q k v o lse
-        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D Dv
         _c_i64p, _c_i64p, _c_i64p, _c_i64p,  # strides
         _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
         _c_void_p, _c_int, _c_int, _c_int, _c_int,  # block_mask n_br n_bc bq bkv
@@ -77,6 +77,13 @@ SIGNATURES: dict[str, tuple] = {
         _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype R Hq Hkv D
         _c_int, _c_int, _c_int,  # num_pages page_size max_pages_per_req
         _c_i64p, _c_i64p, _c_float, _c_float, _c_int,  # q_strides o_strides scale softcap chunks_per_split
+        _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
+    ]),
+    "ffa_mla_decode_workspace_size": (_c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "ffa_mla_decode": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # q ckv bt lens out lse
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype R H num_pages page_size max_pages
+        _c_i64p, _c_i64p, _c_float, _c_int,  # q_strides o_strides scale chunks_per_split
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
     ]),
     "ffa_paged_append": (_c_int, [

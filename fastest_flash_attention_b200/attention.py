@@ -23,7 +23,8 @@ from .config import AttentionConfig
 from .utils import auto_select_block_size, maybe_unsqueeze_head
 
 _KERNEL_DTYPES = (torch.float16, torch.bfloat16)
-SUPPORTED_HEAD_DIMS = (64, 128)
+SUPPORTED_HEAD_DIMS = (64, 128)  # backward
+FWD_HEAD_DIMS = ((64, 64), (128, 128), (192, 128))  # forward (qk, v)
 
 
 def kernel_dtype(t: torch.Tensor, compute_dtype: Optional[torch.dtype] = None) -> torch.dtype:
@@ -61,17 +62,22 @@ def flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
     _lib.require_cuda(q, k, v)
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
-    if k.shape[0] != B or v.shape[:3] != k.shape[:3] or k.shape[3] != D or v.shape[3] != D:
+    Dv = v.shape[3]
+    if k.shape[0] != B or v.shape[:3] != k.shape[:3] or k.shape[3] != D:
         raise ValueError(f"incompatible q/k/v shapes {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
     if Hq % Hkv != 0:
         raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
-    if D not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"head_dim {D} not supported by the sm_100a forward kernel (supported: {SUPPORTED_HEAD_DIMS})")
+    if (D, Dv) not in FWD_HEAD_DIMS:
+        raise ValueError(f"head dims (qk={D}, v={Dv}) not supported by the sm_100a forward kernel "
+                         f"(supported: {FWD_HEAD_DIMS})")
     dt = kernel_dtype(q, compute_dtype)
     q = _tma_ready(q, dt)
     k = _tma_ready(k, dt)
     v = _tma_ready(v, dt)
-    o = torch.empty_like(q)  # keeps q's stride order when q is dense
+    if Dv == D:
+        o = torch.empty_like(q)  # keeps q's stride order when q is dense
+    else:
+        o = torch.empty((B, Sq, Hq, Dv), dtype=dt, device=q.device).transpose(1, 2)
     lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device) if want_lse else None
     bm_ptr, n_br, n_bc = None, 0, 0
     if block_mask is not None:
@@ -82,7 +88,7 @@ def flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
     with torch.cuda.device(q.device):
         st = lib.ffa_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else None,
-            _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D,
+            _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, Dv,
             _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o),
             float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),
             bm_ptr, n_br, n_bc, int(mask_block[0]), int(mask_block[1]),

@@ -37,13 +37,17 @@ constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block m
 constexpr float RESCALE_LOG2 = 8.0f;
 constexpr int FWD_PCH = 4;  // P is handed to the MMA warp in 4 chunks of 32 keys
 
-template <int D>
+// D = query/key head dim, DV = value head dim (DV <= 128; D = 192 with
+// DV = 128 is the MLA prefill shape: 128 "nope" + 64 rotary dims).
+template <int D, int DV>
 struct FwdCfg {
-  static constexpr int TILE = FWD_BM * D * 2;  // bytes of one 128 x D 16-bit tile
-  static constexpr int NBUF = (D == 64) ? 8 : 4;
+  static constexpr int TILE = FWD_BM * D * 2;     // one 128-row Q (or K) tile
+  static constexpr int VTILE = FWD_BN * DV * 2;   // one 128-row V tile
+  static constexpr int BUF = TILE > VTILE ? TILE : VTILE;  // ring slot (holds a K or a V tile)
+  static constexpr int NBUF = (D == 64) ? 8 : (D == 128 ? 4 : 2);
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = FWD_NQT * TILE;
-  static constexpr int BAR_OFF = KV_OFF + NBUF * TILE;
+  static constexpr int BAR_OFF = KV_OFF + NBUF * BUF;
   static constexpr int LIST_OFF = BAR_OFF + 512;
   static constexpr int SMEM = LIST_OFF + FWD_MAX_LIST * 2 + 1024;  // + alignment slack
 };
@@ -93,11 +97,11 @@ __device__ __forceinline__ bool mask_entry(const FwdParams& p, int row, int col)
   return p.block_mask[(size_t)(row / p.mask_bq) * p.n_bc + (col / p.mask_bkv)] != 0;
 }
 
-template <typename T, int D>
+template <typename T, int D, int DV>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
-  using Cfg = FwdCfg<D>;
+  using Cfg = FwdCfg<D, DV>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
@@ -224,10 +228,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&bars->kv_full[buf], Cfg::TILE);
+          mbar_arrive_expect_tx(&bars->kv_full[buf], kv ? Cfg::VTILE : Cfg::TILE);
           ++issued;
-          uint8_t* dst = sKV + buf * Cfg::TILE;
-          for (int c = 0; c < D / 64; ++c)
+          uint8_t* dst = sKV + buf * Cfg::BUF;
+          for (int c = 0; c < (kv ? DV : D) / 64; ++c)
             tma_load_4d(kv ? &tmV : &tmK, &bars->kv_full[buf], dst + c * (FWD_BN * 128), c * 64, j * FWD_BN,
                         hkv, b, pol_kv);
         }
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     // ---------------------------- MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc_qk = make_idesc_f16(FWD_BM, FWD_BN, FMT, 0, 0);
-      const uint32_t idesc_pv = make_idesc_f16(FWD_BM, D, FMT, 0, 1);
+      const uint32_t idesc_pv = make_idesc_f16(FWD_BM, DV, FMT, 0, 1);
       // Descriptors are built once; every MMA then only adds a constant
       // (address >> 4) offset to the low bits, keeping this single issuing
       // thread's instruction count (and so its issue-slot needs) minimal.
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       auto issue_qk = [&](int t, int buf) {
         const uint32_t d = tmem + t * 128;
         const uint64_t qa = q_base + (uint64_t)((t * Cfg::TILE) >> 4);
-        const uint64_t kb = k_base + (uint64_t)((buf * Cfg::TILE) >> 4);
+        const uint64_t kb = k_base + (uint64_t)((buf * Cfg::BUF) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t off = ((ks / 4) * (FWD_BM * 128) + (ks % 4) * 32) >> 4;
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       auto issue_pv = [&](int t, int buf, bool acc, int chunk) {
         const uint32_t d = tmem + 256 + t * 128;
         const uint32_t a = tmem + t * 128;
-        const uint64_t vb = v_base + (uint64_t)((buf * Cfg::TILE) >> 4);
+        const uint64_t vb = v_base + (uint64_t)((buf * Cfg::BUF) >> 4);
         constexpr int KS_PER = FWD_BN / 16 / FWD_PCH;
 #pragma unroll
         for (int kk = 0; kk < KS_PER; ++kk) {
@@ -395,7 +399,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < DV; c += 32) {
           uint32_t ov[32];
           tmem_ld32(tO + c, ov);
           tmem_ld_wait32(ov);
@@ -444,7 +448,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)h * p.o_sh + (size_t)row * p.o_ss;
     const bool store = row < p.Sq;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < DV; c += 32) {
       uint32_t ov[32];
       if (have_o) {
         tmem_ld32(tO + c, ov);
@@ -478,11 +482,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   }
 }
 
-template <typename T, int D>
+template <typename T, int D, int DV>
 static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdParams& p,
                       int grid, cudaStream_t stream) {
-  using Cfg = FwdCfg<D>;
-  auto kern = ffa_fwd_kernel<T, D>;
+  using Cfg = FwdCfg<D, DV>;
+  auto kern = ffa_fwd_kernel<T, D, DV>;
   static bool attr_set = false;
   if (!attr_set) {
     int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
@@ -496,14 +500,14 @@ static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
 }  // namespace ffa
 
 extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B,
-                       int Hq, int Hkv, int Sq, int Skv, int D, const int64_t* q_strides,
+                       int Hq, int Hkv, int Sq, int Skv, int D, int Dv, const int64_t* q_strides,
                        const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, float scale,
                        int causal, int q_offset, int window, float softcap, const uint8_t* block_mask, int n_br,
                        int n_bc, int mask_bq, int mask_bkv, uint32_t* dev_err, void* stream) {
   using namespace ffa;
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides) return FFA_ERR_INVALID_ARG;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv < 0 || Hq % Hkv != 0) return FFA_ERR_INVALID_ARG;
-  if (D != 64 && D != 128) return FFA_ERR_UNSUPPORTED;
+  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128))) return FFA_ERR_UNSUPPORTED;
   if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
   if (Skv > 65535 * FWD_BN) return FFA_ERR_UNSUPPORTED;
   if (block_mask && (n_br <= 0 || n_bc <= 0 || mask_bq <= 0 || mask_bkv <= 0 ||
@@ -548,7 +552,7 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
     st = make_tmap_4d(&mk, k, dt, 2, D, skv_map, Hkv, B, k_strides[2] * 2, k_strides[1] * 2, k_strides[0] * 2, 64,
                       FWD_BN);
   if (!st)
-    st = make_tmap_4d(&mv, v, dt, 2, D, skv_map, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
+    st = make_tmap_4d(&mv, v, dt, 2, Dv, skv_map, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
                       FWD_BN);
   if (st) return st;
 
@@ -556,9 +560,11 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   if (grid > 0x7fffffffLL) return FFA_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FFA_DTYPE_BF16) {
-    if (D == 64) return launch_fwd<__nv_bfloat16, 64>(mq, mk, mv, p, (int)grid, s);
-    return launch_fwd<__nv_bfloat16, 128>(mq, mk, mv, p, (int)grid, s);
+    if (D == 64) return launch_fwd<__nv_bfloat16, 64, 64>(mq, mk, mv, p, (int)grid, s);
+    if (D == 128) return launch_fwd<__nv_bfloat16, 128, 128>(mq, mk, mv, p, (int)grid, s);
+    return launch_fwd<__nv_bfloat16, 192, 128>(mq, mk, mv, p, (int)grid, s);
   }
-  if (D == 64) return launch_fwd<__half, 64>(mq, mk, mv, p, (int)grid, s);
-  return launch_fwd<__half, 128>(mq, mk, mv, p, (int)grid, s);
+  if (D == 64) return launch_fwd<__half, 64, 64>(mq, mk, mv, p, (int)grid, s);
+  if (D == 128) return launch_fwd<__half, 128, 128>(mq, mk, mv, p, (int)grid, s);
+  return launch_fwd<__half, 192, 128>(mq, mk, mv, p, (int)grid, s);
 }

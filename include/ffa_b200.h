@@ -61,8 +61,8 @@ void ffa_set_wait_limit_ns(unsigned long long ns);
 
 /* ----------------------------------------------------------------------------
  * Prefill / training forward.
- *   q  [B, Hq,  Sq,  D ]   k [B, Hkv, Skv, D]   v [B, Hkv, Skv, D]
- *   o  [B, Hq,  Sq,  D ]   lse [B, Hq, Sq] fp32 (natural log), may be NULL
+ *   q  [B, Hq,  Sq,  D ]   k [B, Hkv, Skv, D]   v [B, Hkv, Skv, Dv]
+ *   o  [B, Hq,  Sq,  Dv]   lse [B, Hq, Sq] fp32 (natural log), may be NULL
  * Strides are given as {batch, head, seq} in elements for each tensor.
  * GQA/MQA: Hq % Hkv == 0, query head h reads kv head h / (Hq / Hkv).
  * causal: key j is visible to query i iff j <= i + q_offset.
@@ -70,10 +70,13 @@ void ffa_set_wait_limit_ns(unsigned long long ns);
  * softcap > 0: scores become softcap * tanh(score * scale / softcap).
  * block_mask (uint8 [n_br, n_bc], 1 = keep) masks every (query, key) pair whose
  *   (i / mask_bq, j / mask_bkv) entry is 0; NULL disables it.
- * Supported: D in {64, 128}, dtype f16/bf16.
+ * D is the query/key head dim, Dv the value (and output) head dim.
+ * Supported (D, Dv): (64, 64), (128, 128), (192, 128) — the last is the MLA
+ * prefill shape (modules/flash_mla.py:96-152: 128 + 64 rotary dims, values
+ * not padded).  dtype f16/bf16.
  * ------------------------------------------------------------------------- */
 int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B, int Hq,
-            int Hkv, int Sq, int Skv, int D, const int64_t* q_strides, const int64_t* k_strides,
+            int Hkv, int Sq, int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
             const int64_t* v_strides, const int64_t* o_strides, float scale, int causal, int q_offset,
             int window, float softcap, const uint8_t* block_mask, int n_br, int n_bc, int mask_bq,
             int mask_bkv, uint32_t* dev_err, void* stream);
@@ -144,6 +147,24 @@ int ffa_paged_decode(const void* q, const void* k_pages, const void* v_pages, co
                      int num_pages, int page_size, int max_pages_per_req, const int64_t* q_strides,
                      const int64_t* o_strides, float scale, float softcap, int chunks_per_split, void* workspace,
                      size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * MLA absorbed decode.  Replaces modules/flash_mla.py:116 FastestFlashMLA
+ * forward for one new token per request (the reference re-runs the whole
+ * prefix through up-projections; here W_UK is folded into the query and
+ * W_UV applied to the latent output by the caller).  Multi-query attention
+ * of H = 32 heads over a paged latent cache:
+ *   q [R, H, 576] = [q_nope W_UK (512) | rope(q_rope) (64)] per head
+ *   ckv_pages [num_pages, page_size, 576] = [c_kv (512) | rope(k_rope) (64)]
+ *   out_lat [R, H, 512] = softmax(q . k * scale) c_kv; lse [R, H] (or NULL)
+ * page_size multiple of 16; workspace from ffa_mla_decode_workspace_size().
+ * ------------------------------------------------------------------------- */
+size_t ffa_mla_decode_workspace_size(int R, int H, int max_pages_per_req, int page_size, int chunks_per_split);
+
+int ffa_mla_decode(const void* q, const void* ckv_pages, const int* block_table, const int* ctx_lens, void* out_lat,
+                   float* lse, int dtype, int R, int H, int num_pages, int page_size, int max_pages_per_req,
+                   const int64_t* q_strides, const int64_t* o_strides, float scale, int chunks_per_split,
+                   void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Paged-KV append: scatter new K/V tokens into their (page, offset) slots.

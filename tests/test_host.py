@@ -39,13 +39,13 @@ def test_invalid_arguments_rejected_without_launch():
     from fastest_flash_attention_b200 import _lib
     lib = _lib.load()
     s = _lib.i64arr(0, 0, 0)
-    st = lib.ffa_fwd(None, None, None, None, None, 1, 1, 1, 1, 1, 1, 128, s, s, s, s, 1.0, 0, 0, 0, 0.0,
+    st = lib.ffa_fwd(None, None, None, None, None, 1, 1, 1, 1, 1, 1, 128, 128, s, s, s, s, 1.0, 0, 0, 0, 0.0,
                      None, 0, 0, 0, 0, None, None)
     assert st == _lib.FFA_ERR_INVALID_ARG
-    st = lib.ffa_fwd(1, 1, 1, 16, None, 1, 1, 3, 2, 1, 1, 128, s, s, s, s, 1.0, 0, 0, 0, 0.0,
+    st = lib.ffa_fwd(1, 1, 1, 16, None, 1, 1, 3, 2, 1, 1, 128, 128, s, s, s, s, 1.0, 0, 0, 0, 0.0,
                      None, 0, 0, 0, 0, None, None)
     assert st == _lib.FFA_ERR_INVALID_ARG
-    st = lib.ffa_fwd(1, 1, 1, 16, None, 1, 1, 1, 1, 1, 1, 96, s, s, s, s, 1.0, 0, 0, 0, 0.0,
+    st = lib.ffa_fwd(1, 1, 1, 16, None, 1, 1, 1, 1, 1, 1, 96, 96, s, s, s, s, 1.0, 0, 0, 0, 0.0,
                      None, 0, 0, 0, 0, None, None)
     assert st == _lib.FFA_ERR_UNSUPPORTED
 
