@@ -216,6 +216,104 @@ def run_reference(args, world, rank):
 # GPU arm
 # ----------------------------------------------------------------------------
 
+def _time(fn, iters, dev):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / iters
+
+
+def _time_flushed(fn, iters, dev):
+    """Mean kernel time with L2 flushed (a 256 MB write) before every timed call."""
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        fn()
+    tot = 0.0
+    for _ in range(iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        tot += e0.elapsed_time(e1)
+    return tot / iters
+
+
+def paged_decode_inputs(dev, seed=0):
+    """Config 4: 64 requests, ctx ~ U[512, 32768], page 16, Hq 32 / Hkv 8, D 128,
+    pool pages shuffled by the seed (permuted block table)."""
+    g = torch.Generator().manual_seed(seed)
+    R, Hq, Hkv, D, PS = 64, 32, 8, 128, 16
+    lens = torch.randint(512, 32769, (R,), generator=g)
+    npg = (lens + PS - 1) // PS
+    P = int(npg.sum())
+    perm = torch.randperm(P, generator=g).to(torch.int32)
+    bt = torch.zeros(R, int(npg.max()), dtype=torch.int32)
+    off = 0
+    for r in range(R):
+        bt[r, :npg[r]] = perm[off:off + npg[r]]
+        off += int(npg[r])
+    kp = torch.randn(P, Hkv, PS, D, device=dev, dtype=torch.bfloat16)
+    vp = torch.randn(P, Hkv, PS, D, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(R, Hq, D, device=dev, dtype=torch.bfloat16)
+    return q, kp, vp, bt.to(dev), lens.to(torch.int32).to(dev), int(lens.sum()), int(lens.max())
+
+
+def secondary_lines(dev, peaks, peak_src):
+    """The other kernels of the path on their BASELINE configs, timed with CUDA
+    events (inputs resident in HBM; each workload exceeds L2)."""
+    from fastest_flash_attention_b200.attention import flash_bwd, flash_fwd
+    from fastest_flash_attention_b200 import paged_decode
+    from fastest_flash_attention_b200.mla import mla_decode
+    pk = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    out = {}
+    # config 3: training fwd+bwd, causal + window 1024 + softcap 30, deterministic
+    B, H, S, D = 8, 16, 4096, 128
+    g = torch.Generator(device=dev).manual_seed(3)
+    q, k, v, do = (torch.randn(B, H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
+    sc = 1 / math.sqrt(D)
+    o, lse = flash_fwd(q, k, v, scale=sc, causal=True, window=1024, softcap=30.0)
+    f_ms = _time(lambda: flash_fwd(q, k, v, scale=sc, causal=True, window=1024, softcap=30.0), 10, dev)
+    b_ms = _time(lambda: flash_bwd(do, q, k, v, o, lse, scale=sc, causal=True, window=1024, softcap=30.0), 10, dev)
+    pairs = 1024 * 1025 // 2 + (S - 1024) * 1024
+    ff = 4.0 * D * pairs * B * H
+    out["train_fwd_bwd_cfg3"] = {
+        "workload": "B=8 H=16 S=4096 D=128 causal+window1024+softcap30, deterministic bwd",
+        "fwd_ms": f_ms, "bwd_ms": b_ms, "fwd_tflops": ff / f_ms / 1e9, "bwd_tflops": 2.5 * ff / b_ms / 1e9,
+        "fwd_bwd_tflops": 3.5 * ff / (f_ms + b_ms) / 1e9,
+        "frac_of_peak": 3.5 * ff / (f_ms + b_ms) / 1e9 / pk, "peak": f"{pk} TFLOP/s ({peak_src} bf16)"}
+    del q, k, v, do, o, lse
+    # config 4: paged decode
+    q, kp, vp, bt, lens, tot, mx = paged_decode_inputs(dev)
+    d_ms = _time(lambda: paged_decode(q, kp, vp, bt, lens, max_ctx=mx), 20, dev)
+    byts = tot * 8 * 128 * 2 * 2 + q.numel() * 2 * 2
+    out["paged_decode_cfg4"] = {
+        "workload": "64 req, ctx U[512,32768], page 16, Hq 32 / Hkv 8, D 128, bf16, permuted block table",
+        "ms": d_ms, "gbs": byts / d_ms / 1e6, "frac_of_hbm": byts / d_ms / 1e6 / hbm,
+        "bytes": byts, "peak": f"{hbm} GB/s ({peak_src})"}
+    del q, kp, vp
+    # config 5: MLA absorbed decode step, B=16 at context 4096 (latent 512 + rope 64, 32 heads)
+    R, L, PS = 16, 4096, 64
+    cache = torch.randn(R * L // PS, PS, 576, device=dev, dtype=torch.bfloat16)
+    btm = torch.arange(R * L // PS, dtype=torch.int32, device=dev).view(R, L // PS)
+    lm = torch.full((R,), L, dtype=torch.int32, device=dev)
+    qm = torch.randn(R, 32, 576, device=dev, dtype=torch.bfloat16)
+    m_ms = _time_flushed(lambda: mla_decode(qm, cache, btm, lm, scale=1 / math.sqrt(192), max_ctx=L), 20, dev)
+    mb = R * L * 576 * 2
+    out["mla_decode_cfg5"] = {"workload": "16 req x ctx 4096, latent 512 + rope 64, 32 heads, bf16", "ms": m_ms,
+                              "gbs": mb / m_ms / 1e6, "frac_of_hbm": mb / m_ms / 1e6 / hbm,
+                              "l2": "cache (75 MB) fits L2: flushed before every timed call"}
+    return out
+
+
 def run_ours(args, world, rank, local):
     from fastest_flash_attention_b200 import fastest_flash_attn_forward
     from fastest_flash_attention_b200.attention import flash_fwd
@@ -315,6 +413,10 @@ def run_ours(args, world, rank, local):
                      "algorithmic_flops_per_launch": flops},
         "clocks": clk.summary(),
     }
+    if not args.no_secondary:
+        del q, k, v
+        torch.cuda.empty_cache()
+        line["secondary"] = secondary_lines(dev, peaks, peak_src)
     if world == 1:
         runs = [cpu_reference_sample(q_h, k_h, v_h) for _ in range(3)]
         tfc = statistics.median(r[0] for r in runs)
@@ -322,6 +424,35 @@ def run_ours(args, world, rank, local):
                                 "sample": runs[0][2] + ", median of 3",
                                 "seconds": sum(r[1] for r in runs)}
     print(json.dumps(line), flush=True)
+
+
+def run_profile(args):
+    """Capture-sized cases (inputs above L2, a few GB at most) for ncu."""
+    from fastest_flash_attention_b200.attention import flash_bwd, flash_fwd
+    from fastest_flash_attention_b200 import paged_decode
+    from fastest_flash_attention_b200.mla import mla_decode
+    dev = torch.device("cuda", 0)
+    n = args.warmup + args.steps
+    if args.profile == "bwd":
+        B, H, S, D = 2, 16, 4096, 128
+        q, k, v, do = (torch.randn(B, H, S, D, device=dev).to(torch.bfloat16) for _ in range(4))
+        o, lse = flash_fwd(q, k, v, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
+        for _ in range(n):
+            flash_bwd(do, q, k, v, o, lse, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
+    elif args.profile == "decode":
+        q, kp, vp, bt, lens, tot, mx = paged_decode_inputs(dev)
+        for _ in range(n):
+            paged_decode(q, kp, vp, bt, lens, max_ctx=mx)
+    else:
+        R, L, PS = 16, 4096, 64
+        cache = torch.randn(R * L // PS, PS, 576, device=dev, dtype=torch.bfloat16)
+        bt = torch.arange(R * L // PS, dtype=torch.int32, device=dev).view(R, L // PS)
+        lens = torch.full((R,), L, dtype=torch.int32, device=dev)
+        qm = torch.randn(R, 32, 576, device=dev, dtype=torch.bfloat16)
+        for _ in range(n):
+            mla_decode(qm, cache, bt, lens, scale=192 ** -0.5, max_ctx=L)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.profile, "launches": n}))
 
 
 def main():
@@ -332,9 +463,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["full", "small"], default="full")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
+    ap.add_argument("--profile", choices=["bwd", "decode", "mla"], default=None,
+                    help="run only that kernel family a few times on a capture-sized case (for ncu)")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the other kernels' lines")
     args = ap.parse_args()
     if args.case == "small":
         CFG.update(SMALL_CFG)
+    if args.profile:
+        run_profile(args)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_init()
     try:
