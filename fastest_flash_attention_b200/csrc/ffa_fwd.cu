@@ -27,10 +27,15 @@ namespace ffa {
 constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
 constexpr int FWD_NQT = 2;    // query tiles per CTA
 constexpr int FWD_BN = 128;   // keys per key tile
-constexpr int FWD_THREADS = 256;  // two softmax warpgroups; no separate TMA / MMA warps
-constexpr int FWD_WARP_TMEM = 1;  // allocates / frees TMEM
+constexpr int FWD_THREADS = 384;  // 2 softmax warpgroups + 1 warpgroup for TMA / MMA (2 warps idle)
+// Register budgets after the split: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
+constexpr uint32_t FWD_REGS_SOFTMAX = 208;
+constexpr uint32_t FWD_REGS_OTHER = 88;
+constexpr int FWD_WARP_LOAD = 8;
+constexpr int FWD_WARP_MMA = 9;
 constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block mask filters them
 constexpr float RESCALE_LOG2 = 8.0f;
+constexpr int FWD_PCH = 4;  // P is handed to the MMA warp in 4 chunks of 32 keys
 
 // D = query/key head dim, DV = value head dim (DV <= 128; D = 192 with
 // DV = 128 is the MLA prefill shape: 128 "nope" + 64 rotary dims).
@@ -66,9 +71,9 @@ struct FwdParams {
 struct FwdBars {
   uint64_t q_full;
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_full[2][FWD_PCH];
   uint64_t o_done[2];
-  uint64_t drain[2];
+  uint64_t drain;
   uint64_t kv_full[8];
   uint64_t kv_empty[8];
   uint32_t tmem_base;
@@ -88,9 +93,6 @@ enum : uint32_t {
   SITE_FWD_DRAIN = 0x107,
 };
 
-__device__ __forceinline__ bool mask_entry(const FwdParams& p, int row, int col) {
-  return p.block_mask[(size_t)(row / p.mask_bq) * p.n_bc + (col / p.mask_bkv)] != 0;
-}
 
 template <typename T, int D, int DV>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -128,22 +130,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     mbar_init(&bars->q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], FWD_BM);
+      for (int k = 0; k < FWD_PCH; ++k) mbar_init(&bars->p_full[t][k], FWD_BM);
       mbar_init(&bars->o_done[t], 1);
-      mbar_init(&bars->drain[t], 1);
     }
+    mbar_init(&bars->drain, 1);
     for (int i = 0; i < Cfg::NBUF; ++i) {
       mbar_init(&bars->kv_full[i], 1);
-      mbar_init(&bars->kv_empty[i], FWD_NQT);  // released once by each query tile's issuer
+      mbar_init(&bars->kv_empty[i], 1);
     }
     bars->abort = 0;
     fence_mbar_init();
   }
-  if (warp == FWD_WARP_TMEM) {
+  if (warp == FWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
-  if (warp == 0) {
+  if (warp == FWD_WARP_LOAD) {
     // Key-tile range allowed by causal / window masks, then filtered by the
     // block mask (a tile stays if any of its (row, col) pairs is kept).
     int j_hi = n_kv;
@@ -196,285 +198,308 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   auto tile_at = [&](int it) -> int { return use_list ? (int)list[it] : j_lo + it; };
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  const int t = warp / 4;           // query tile of this warpgroup
-  const int r = threadIdx.x % FWD_BM;
-  const bool issuer = (r == 0);     // issues this tile's MMAs
-  const bool loader = (threadIdx.x == 0);  // also streams Q, K, V with TMA
-
-  // ------------------------------- loader ----------------------------------
-  // Thread 0 keeps the K/V ring full without ever blocking on it: `pump`
-  // issues every load whose slot has been released, and every wait this
-  // thread performs keeps pumping.
-  const uint64_t pol_kv = policy_evict_last();
-  int ld_next = 0;  // next K/V slot (2 per key tile: K then V)
-  auto pump = [&]() {
-    while (ld_next < 2 * n) {
-      const int s = ld_next, buf = s % Cfg::NBUF, use = s / Cfg::NBUF;
-      if (use > 0 && !mbar_test(&bars->kv_empty[buf], (use - 1) & 1)) break;
-      const int kv = s & 1, j = tile_at(s >> 1);
-      mbar_arrive_expect_tx(&bars->kv_full[buf], kv ? Cfg::VTILE : Cfg::TILE);
-      uint8_t* dst = sKV + buf * Cfg::BUF;
-      for (int c = 0; c < (kv ? DV : D) / 64; ++c)
-        tma_load_4d(kv ? &tmV : &tmK, &bars->kv_full[buf], dst + c * (FWD_BN * 128), c * 64, j * FWD_BN, hkv, b,
-                    pol_kv);
-      ++ld_next;
-    }
-  };
-  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t site) -> bool {
-    if (!loader) return mbar_wait(bar, par, p.ec, abort_flag, site);
-    if (mbar_test(bar, par)) return true;
-    const long long t0 = clock64(), limit = (long long)(p.ec.limit_ns * 2ull);
-    while (true) {
-      pump();
-      if (mbar_test(bar, par)) return true;
-      if (*abort_flag) return false;
-      if (clock64() - t0 > limit) {
-        *abort_flag = 1;
-        if (p.ec.err) atomicCAS(p.ec.err, 0u, site);
-        return false;
+  if (warp >= 8) {
+   regs_dec<FWD_REGS_OTHER>();
+   if (warp == FWD_WARP_LOAD) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(&bars->q_full, FWD_NQT * Cfg::TILE);
+      for (int t = 0; t < FWD_NQT; ++t)
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(&tmQ, &bars->q_full, sQ + t * Cfg::TILE + c * (FWD_BM * 128), c * 64, q_lo + t * FWD_BM,
+                      h, b, pol_q);
+      int issued = 0;  // key/value slots armed so far
+      for (int it = 0; it < n; ++it) {
+        const int j = tile_at(it);
+        bool ok = true;
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          const int s = 2 * it + kv;
+          const int buf = s % Cfg::NBUF;
+          const int use = s / Cfg::NBUF;
+          if (use > 0 && !mbar_wait(&bars->kv_empty[buf], (use - 1) & 1, p.ec, abort_flag, SITE_FWD_KV_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->kv_full[buf], kv ? Cfg::VTILE : Cfg::TILE);
+          ++issued;
+          uint8_t* dst = sKV + buf * Cfg::BUF;
+          for (int c = 0; c < (kv ? DV : D) / 64; ++c)
+            tma_load_4d(kv ? &tmV : &tmK, &bars->kv_full[buf], dst + c * (FWD_BN * 128), c * 64, j * FWD_BN,
+                        hkv, b, pol_kv);
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // Let copies still in flight land before the CTA gives up its smem.
+        mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+        for (int s = max(0, issued - Cfg::NBUF); s < issued; ++s)
+          mbar_wait(&bars->kv_full[s % Cfg::NBUF], (s / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_DRAIN, true);
       }
     }
-  };
-  if (loader && n > 0) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-    const uint64_t pol_q = policy_evict_first();
-    mbar_arrive_expect_tx(&bars->q_full, FWD_NQT * Cfg::TILE);
-    for (int tq = 0; tq < FWD_NQT; ++tq)
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_4d(&tmQ, &bars->q_full, sQ + tq * Cfg::TILE + c * (FWD_BM * 128), c * 64, q_lo + tq * FWD_BM, h, b,
-                    pol_q);
-    pump();
-  }
-
-  // ------------------------------- MMA issue -------------------------------
-  const uint32_t idesc_qk = make_idesc_f16(FWD_BM, FWD_BN, FMT, 0, 0);
-  const uint32_t idesc_pv = make_idesc_f16(FWD_BM, DV, FMT, 0, 1);
-  const uint32_t tS0 = tmem + t * 128;        // lane-0 TMEM addresses of this tile's S/P and O
-  const uint32_t tO0 = tmem + 256 + t * 128;
-  auto issue_qk = [&](int buf) {
-    const uint64_t qa = make_sdesc_sw128(smem_u32(sQ + t * Cfg::TILE), 16, 1024);
-    const uint64_t kb = make_sdesc_sw128(smem_u32(sKV + buf * Cfg::BUF), 16, 1024);
+    __syncwarp();
+  } else if (warp == FWD_WARP_MMA) {
+    // ---------------------------- MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc_f16(FWD_BM, FWD_BN, FMT, 0, 0);
+      const uint32_t idesc_pv = make_idesc_f16(FWD_BM, DV, FMT, 0, 1);
+      // Descriptors are built once; every MMA then only adds a constant
+      // (address >> 4) offset to the low bits, keeping this single issuing
+      // thread's instruction count (and so its issue-slot needs) minimal.
+      const uint64_t q_base = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_base = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
+      const uint64_t v_base = make_sdesc_sw128(smem_u32(sKV), FWD_BN * 128, 1024);
+      auto issue_qk = [&](int t, int buf) {
+        const uint32_t d = tmem + t * 128;
+        const uint64_t qa = q_base + (uint64_t)((t * Cfg::TILE) >> 4);
+        const uint64_t kb = k_base + (uint64_t)((buf * Cfg::BUF) >> 4);
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const uint32_t off = ((ks / 4) * (FWD_BM * 128) + (ks % 4) * 32) >> 4;
-      mma_ss(tS0, qa + off, kb + off, idesc_qk, ks > 0);
-    }
-  };
-  auto issue_pv = [&](int buf, bool acc) {
-    const uint64_t vb = make_sdesc_sw128(smem_u32(sKV + buf * Cfg::BUF), FWD_BN * 128, 1024);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = ((ks / 4) * (FWD_BM * 128) + (ks % 4) * 32) >> 4;
+          mma_ss(d, qa + off, kb + off, idesc_qk, ks > 0);
+        }
+      };
+      // P·V for one chunk of keys (k-steps of 16 keys); chunks are issued as
+      // the softmax group releases them.
+      auto issue_pv = [&](int t, int buf, bool acc, int chunk) {
+        const uint32_t d = tmem + 256 + t * 128;
+        const uint32_t a = tmem + t * 128;
+        const uint64_t vb = v_base + (uint64_t)((buf * Cfg::BUF) >> 4);
+        constexpr int KS_PER = FWD_BN / 16 / FWD_PCH;
 #pragma unroll
-    for (int ks = 0; ks < FWD_BN / 16; ++ks)
-      mma_ts(tO0, tS0 + ks * 8, vb + (uint64_t)((ks * 16 * 128) >> 4), idesc_pv, (acc || ks > 0) ? 1u : 0u);
-  };
-  if (issuer && n > 0) {
-    if (wait(&bars->q_full, 0, SITE_FWD_Q) && wait(&bars->kv_full[0], 0, SITE_FWD_KV_FULL)) {
-      tc_fence_after();
-      issue_qk(0);
-      mma_commit(&bars->s_full[t]);
-      mma_commit(&bars->kv_empty[0]);
-    }
-  }
-  __syncwarp();
-
-  // -------------------------------- softmax --------------------------------
-  const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-  const uint32_t tS = tmem + lane_off + t * 128;
-  const uint32_t tO = tmem + lane_off + 256 + t * 128;
-  const int row = q_lo + t * FWD_BM + r;
-  const int arow = row + p.q_offset;
-  float m = -INFINITY, l = 0.f;
-  bool ok = true;
-  for (int it = 0; it < n; ++it) {
-    const int j = tile_at(it);
-    ok = __all_sync(0xffffffffu, wait(&bars->s_full[t], it & 1, SITE_FWD_S_FULL));
-    if (!ok) break;
-    tc_fence_after();
-    uint32_t s[FWD_BN];
-#pragma unroll
-    for (int c = 0; c < FWD_BN; c += 32) tmem_ld32(tS + c, s + c);
-#pragma unroll
-    for (int c = 0; c < FWD_BN; c += 32) tmem_ld_wait32(s + c);
-    // Scores in base-2 units: s * scale*log2(e), or with a softcap
-    // softcap*tanh(s*scale/softcap)*log2(e) computed in place (then mul = 1).
-    float mul = p.scale_log2;
-    if (p.use_softcap) {
-#pragma unroll
-      for (int c = 0; c < FWD_BN; ++c)
-        s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
-      mul = 1.f;
-    }
-    const int c0 = j * FWD_BN;
-    const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) || (p.window > 0 && c0 < a_hi - p.window + 1) ||
-                           (c0 + FWD_BN > p.Skv) || (p.block_mask != nullptr);
-    if (need_mask) {
-      // Visible keys of this row form one range [lo, hi] (causal / window /
-      // sequence end); one unsigned compare per element, no branches.
-      const int hi = min(p.causal ? arow : 0x7ffffffe, p.Skv - 1) - c0;
-      const int lo_c = p.window > 0 ? max(arow - p.window + 1 - c0, 0) : 0;
-      const uint32_t span = hi >= lo_c ? (uint32_t)(hi - lo_c) : 0xffffffffu;
-      const uint32_t ninf = __float_as_uint(-INFINITY);
-#pragma unroll
-      for (int c = 0; c < FWD_BN; ++c) {
-        const bool keep = span != 0xffffffffu && (uint32_t)(c - lo_c) <= span;
-        s[c] = keep ? s[c] : ninf;
+        for (int kk = 0; kk < KS_PER; ++kk) {
+          const int ks = chunk * KS_PER + kk;
+          mma_ts(d, a + ks * 8, vb + (uint64_t)((ks * 16 * 128) >> 4), idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = n == 0 || mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_Q);
+      if (ok && n > 0) {
+        ok = mbar_wait(&bars->kv_full[0], 0, p.ec, abort_flag, SITE_FWD_KV_FULL);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0, 0);
+          mma_commit(&bars->s_full[0]);
+          issue_qk(1, 0);
+          mma_commit(&bars->s_full[1]);
+          mma_commit(&bars->kv_empty[0]);
+        }
       }
-      if (p.block_mask != nullptr) {
-        // Column keep-bits of this row from the block mask (a runtime loop over
-        // the mask blocks the tile touches), then applied with an unrolled
-        // bit test so s[] stays in registers.
-        const uint8_t* mrow = p.block_mask + (size_t)(min(row, p.Sq - 1) / p.mask_bq) * p.n_bc;
-        uint32_t kb[4] = {~0u, ~0u, ~0u, ~0u};
-#pragma unroll 1
-        for (int bc = c0 / p.mask_bkv; bc * p.mask_bkv < c0 + FWD_BN && bc < p.n_bc; ++bc) {
-          if (mrow[bc]) continue;
-          const int clo = max(bc * p.mask_bkv - c0, 0), chi = min((bc + 1) * p.mask_bkv - c0, FWD_BN);
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const int a = max(clo, 32 * w), e = min(chi, 32 * w + 32);
-            if (a < e) {
-              const uint32_t len = e - a;
-              const uint32_t bits = (len == 32 ? ~0u : ((1u << len) - 1u)) << (a - 32 * w);
-              kb[w] &= ~bits;
+      for (int it = 0; it < n && ok; ++it) {
+        const int vs = 2 * it + 1, vb = vs % Cfg::NBUF;
+        const bool has_next = it + 1 < n;
+        const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
+        if (!mbar_wait(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
+        for (int t = 0; t < FWD_NQT && ok; ++t) {
+          for (int k = 0; k < FWD_PCH; ++k) {
+            if (!mbar_wait(&bars->p_full[t][k], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            issue_pv(t, vb, it > 0, k);
+          }
+          if (!ok) break;
+          mma_commit(&bars->o_done[t]);
+          if (has_next) {
+            if (t == 0 && !mbar_wait(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(t, kb);
+            mma_commit(&bars->s_full[t]);
           }
         }
-#pragma unroll
-        for (int c = 0; c < FWD_BN; ++c) s[c] = ((kb[c / 32] >> (c % 32)) & 1u) ? s[c] : ninf;
+        if (!ok) break;
+        mma_commit(&bars->kv_empty[vb]);
+        if (has_next) mma_commit(&bars->kv_empty[kb]);
       }
+      // Every MMA must retire before TMEM is released.
+      mma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
     }
-    // Row max: eight independent 3-input max chains, then a small tree.
-    float mx[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[i]);
-#pragma unroll
-    for (int c = 8; c < FWD_BN; c += 16)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
-    const float mraw = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-    const float m_new = fmaxf(m, mraw * mul);
-    const bool warp_resc = __any_sync(0xffffffffu, m_new > m + RESCALE_LOG2);
-    float alpha = 1.f;
-    if (warp_resc) {
-      alpha = (m_new == -INFINITY) ? 1.f : ex2(m - m_new);
-      l *= alpha;
-      m = m_new;
-    }
-    // O must carry the new max before this tile's P.V accumulates into it.
-    // P.V of the previous tile was issued before this tile's Q.K^T by the same
-    // thread, so it retired before S became ready: the wait is immediate.
-    if (warp_resc && it > 0) {
-      ok = __all_sync(0xffffffffu, wait(&bars->o_done[t], (it - 1) & 1, SITE_FWD_O_DONE));
+    __syncwarp();
+   }
+  } else {
+    regs_inc<FWD_REGS_SOFTMAX>();
+    // ------------------------------ softmax -------------------------------
+    const int t = warp / 4;
+    const int r = threadIdx.x % FWD_BM;
+    const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const int row = q_lo + t * FWD_BM + r;
+    const int arow = row + p.q_offset;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int it = 0; it < n; ++it) {
+      const int j = tile_at(it);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], it & 1, p.ec, abort_flag, SITE_FWD_S_FULL));
       if (!ok) break;
       tc_fence_after();
+      uint32_t s[FWD_BN];
 #pragma unroll
-      for (int c = 0; c < DV; c += 32) {
-        uint32_t ov[32];
-        tmem_ld32(tO + c, ov);
-        tmem_ld_wait32(ov);
+      for (int c = 0; c < FWD_BN; c += 32) tmem_ld32(tS + c, s + c);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-        tmem_st32(tO + c, ov);
+      for (int c = 0; c < FWD_BN; c += 32) tmem_ld_wait32(s + c);
+      // Scores in base-2 units are  s * mul  (mul = scale*log2 e), or, with a
+      // softcap, softcap*tanh(s*scale/softcap)*log2 e computed in place (mul = 1).
+      float mul = p.scale_log2;
+      if (p.use_softcap) {
+#pragma unroll
+        for (int c = 0; c < FWD_BN; ++c)
+          s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+        mul = 1.f;
       }
-    }
-    const float mu = (m == -INFINITY) ? 0.f : m;
-    const float2 mul2 = make_float2(mul, mul);
-    const float2 nmu2 = make_float2(-mu, -mu);
-    // p = 2^(s*mul - mu), packed to 16-bit pairs and written over S in TMEM.
-    float2 acc[4];
+      const int c0 = j * FWD_BN;
+      const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) ||
+                             (p.window > 0 && c0 < a_hi - p.window + 1) || (c0 + FWD_BN > p.Skv) ||
+                             (p.block_mask != nullptr);
+      if (need_mask) {
+        // Visible keys of this row form one range [lo_c, hi] (causal, window
+        // and sequence end): one unsigned compare per element, no branches.
+        // (A branchy per-element form made the compiler keep s[] in local
+        // memory and ran ~30x slower on these diagonal tiles.)
+        const int hi = min(p.causal ? arow : 0x7ffffffe, p.Skv - 1) - c0;
+        const int lo_c = p.window > 0 ? max(arow - p.window + 1 - c0, 0) : 0;
+        const uint32_t span = hi >= lo_c ? (uint32_t)(hi - lo_c) : 0xffffffffu;
+        const uint32_t ninf = __float_as_uint(-INFINITY);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
-    uint32_t pk[FWD_BN / 2];
+        for (int c = 0; c < FWD_BN; ++c) {
+          const bool keep = span != 0xffffffffu && (uint32_t)(c - lo_c) <= span;
+          s[c] = keep ? s[c] : ninf;
+        }
+        if (p.block_mask != nullptr) {
+          // Column keep-bits of this row from the block mask (a runtime loop
+          // over the mask blocks the tile touches), applied with an unrolled
+          // bit test so s[] stays in registers.
+          const uint8_t* mrow = p.block_mask + (size_t)(min(row, p.Sq - 1) / p.mask_bq) * p.n_bc;
+          uint32_t kb[4] = {~0u, ~0u, ~0u, ~0u};
+#pragma unroll 1
+          for (int bc = c0 / p.mask_bkv; bc * p.mask_bkv < c0 + FWD_BN && bc < p.n_bc; ++bc) {
+            if (mrow[bc]) continue;
+            const int clo = max(bc * p.mask_bkv - c0, 0), chi = min((bc + 1) * p.mask_bkv - c0, FWD_BN);
 #pragma unroll
-    for (int c = 0; c < FWD_BN / 2; ++c) {
-      const float2 a = ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), mul2, nmu2);
-      float2 pv;
-      pv.x = ex2(a.x);
-      pv.y = ex2(a.y);
-      acc[c & 3] = fadd2(acc[c & 3], pv);
-      pk[c] = pack2<T>(pv.x, pv.y);
-    }
-    const float2 acct = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
-    l += acct.x + acct.y;
-    tmem_st32(tS, pk);
-    tmem_st32(tS + 32, pk + 32);
-    tmem_st_wait();
-    tc_fence_before();
-    mbar_arrive(&bars->p_full[t]);
-    // The issuer waits for the whole group's P, then issues P.V for this tile
-    // and Q.K^T for the next (which overwrites S/P: the tensor core executes
-    // one thread's MMAs in issue order).
-    if (issuer) {
-      const int vs = 2 * it + 1, vb = vs % Cfg::NBUF;
-      if (wait(&bars->p_full[t], it & 1, SITE_FWD_P_FULL) &&
-          wait(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, SITE_FWD_KV_FULL)) {
-        tc_fence_after();
-        issue_pv(vb, it > 0);
-        mma_commit(&bars->o_done[t]);
-        mma_commit(&bars->kv_empty[vb]);
-        if (it + 1 < n) {
-          const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
-          if (wait(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, SITE_FWD_KV_FULL)) {
-            tc_fence_after();
-            issue_qk(kb);
-            mma_commit(&bars->s_full[t]);
-            mma_commit(&bars->kv_empty[kb]);
+            for (int w = 0; w < 4; ++w) {
+              const int a = max(clo, 32 * w), e = min(chi, 32 * w + 32);
+              if (a < e) {
+                const uint32_t len = e - a;
+                kb[w] &= ~((len == 32 ? ~0u : ((1u << len) - 1u)) << (a - 32 * w));
+              }
+            }
           }
+#pragma unroll
+          for (int c = 0; c < FWD_BN; ++c) s[c] = ((kb[c / 32] >> (c % 32)) & 1u) ? s[c] : ninf;
         }
       }
+      // Row max: eight independent 3-input max chains, then a small tree.
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[i]);
+#pragma unroll
+      for (int c = 8; c < FWD_BN; c += 16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
+      const float mraw = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float m_new = fmaxf(m, mraw * mul);
+      const bool warp_resc = __any_sync(0xffffffffu, m_new > m + RESCALE_LOG2);
+      float alpha = 1.f;
+      if (warp_resc) {
+        alpha = (m_new == -INFINITY) ? 1.f : ex2(m - m_new);
+        l *= alpha;
+        m = m_new;
+      }
+      // O must carry the new max before this tile's P·V accumulates into it.
+      // P·V of the previous tile retired before this tile's S was produced
+      // (the tensor core runs in issue order), so the wait below is immediate.
+      if (warp_resc && it > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bars->o_done[t], (it - 1) & 1, p.ec, abort_flag, SITE_FWD_O_DONE));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < DV; c += 32) {
+          uint32_t ov[32];
+          tmem_ld32(tO + c, ov);
+          tmem_ld_wait32(ov);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(tO + c, ov);
+        }
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      const float2 mul2 = make_float2(mul, mul);
+      const float2 nmu2 = make_float2(-mu, -mu);
+      // p = 2^(s*mul - mu), written over S as 16-bit pairs one 32-key chunk at
+      // a time; each chunk is released to the MMA warp as soon as it is in
+      // TMEM so P·V overlaps the rest of the exponentials.
+      float2 acc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < FWD_PCH; ++k) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int c = k * 16 + e;
+          const float2 a =
+              ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), mul2, nmu2);
+          float2 pv;
+          pv.x = ex2(a.x);
+          pv.y = ex2(a.y);
+          acc[e & 3] = fadd2(acc[e & 3], pv);
+          pk[e] = pack2<T>(pv.x, pv.y);
+        }
+        tmem_st16(tS + k * 16, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[t][k]);
+      }
+      const float2 acct = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+      l += acct.x + acct.y;
     }
-    if (loader) pump();
-    __syncwarp();
-  }
-  if (issuer) {
-    // Every MMA of this tile retires before TMEM is released.
-    mma_commit(&bars->drain[t]);
-    mbar_wait(&bars->drain[t], 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
-  }
-  if (loader && *abort_flag) {
-    // Let copies still in flight land before the CTA gives up its smem.
-    if (n > 0) mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
-    for (int s2 = max(0, ld_next - Cfg::NBUF); s2 < ld_next; ++s2)
-      mbar_wait(&bars->kv_full[s2 % Cfg::NBUF], (s2 / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_DRAIN, true);
-  }
-  __syncwarp();
-  // ------------------------------ epilogue --------------------------------
-  const bool have_o = ok && n > 0 &&
-                      __all_sync(0xffffffffu, mbar_wait(&bars->o_done[t], (n - 1) & 1, p.ec, abort_flag, SITE_FWD_O_DONE));
-  if (have_o) tc_fence_after();
-  const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-  T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)h * p.o_sh + (size_t)row * p.o_ss;
-  const bool store = row < p.Sq;
+    // ------------------------------ epilogue ------------------------------
+    const bool have_o =
+        ok && n > 0 &&
+        __all_sync(0xffffffffu, mbar_wait(&bars->o_done[t], (n - 1) & 1, p.ec, abort_flag, SITE_FWD_O_DONE));
+    if (have_o) tc_fence_after();
+    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)h * p.o_sh + (size_t)row * p.o_ss;
+    const bool store = row < p.Sq;
 #pragma unroll
-  for (int c = 0; c < DV; c += 32) {
-    uint32_t ov[32];
-    if (have_o) {
-      tmem_ld32(tO + c, ov);
-      tmem_ld_wait32(ov);
-    } else {
+    for (int c = 0; c < DV; c += 32) {
+      uint32_t ov[32];
+      if (have_o) {
+        tmem_ld32(tO + c, ov);
+        tmem_ld_wait32(ov);
+      } else {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) ov[e] = 0u;
+        for (int e = 0; e < 32; ++e) ov[e] = 0u;
+      }
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        pk[e] = pack2<T>(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
+      if (store) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+      }
     }
-    uint32_t pk[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e)
-      pk[e] = pack2<T>(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
-    if (store) {
-      uint4* dst = reinterpret_cast<uint4*>(orow + c);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+    if (store && p.lse != nullptr) {
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      const float lse = (l > 0.f) ? (mu + lg2(l)) * 0.6931471805599453f : -INFINITY;
+      p.lse[((size_t)b * p.Hq + h) * p.Sq + row] = lse;
     }
-  }
-  if (store && p.lse != nullptr) {
-    const float mu = (m == -INFINITY) ? 0.f : m;
-    const float lse = (l > 0.f) ? (mu + lg2(l)) * 0.6931471805599453f : -INFINITY;
-    p.lse[((size_t)b * p.Hq + h) * p.Sq + row] = lse;
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == FWD_WARP_TMEM) {
+  if (warp == FWD_WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
