@@ -345,6 +345,19 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   return r;
 }
 
+// tanh on |x| <= 1/2 by its Taylor series to x^11 (odd terms; coefficients
+// 1, -1/3, 2/15, -17/315, 62/2835, -1382/155925).  The first omitted term
+// bounds the error: 21844/6081075 * 2^-13 < 4.4e-7.  FMA pipe only.
+__device__ __forceinline__ float tanh_small(float x) {
+  const float x2 = x * x;
+  float p = -8.8632e-3f;                    // -1382/155925
+  p = fmaf(p, x2, 2.1869488536155203e-2f);  //  62/2835
+  p = fmaf(p, x2, -5.3968253968253971e-2f); // -17/315
+  p = fmaf(p, x2, 1.3333333333333333e-1f);  //  2/15
+  p = fmaf(p, x2, -3.3333333333333333e-1f); // -1/3
+  return fmaf(p * x2, x, x);
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
 template <>

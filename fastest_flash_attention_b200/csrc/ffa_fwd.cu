@@ -350,9 +350,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       // softcap, softcap*tanh(s*scale/softcap)*log2 e computed in place (mul = 1).
       float mul = p.scale_log2;
       if (p.use_softcap) {
+        // tanh(s*scale/softcap): the FMA-pipe series when every argument of
+        // the warp's tile is within 1/2 (the usual case, softcap >> scores),
+        // else the exact exp-based form (two MUFU ops per score).
+        float amax = 0.f;
 #pragma unroll
-        for (int c = 0; c < FWD_BN; ++c)
-          s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+        for (int c = 0; c < FWD_BN; c += 2)
+          amax = fmax3(amax, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
+        if (__all_sync(0xffffffffu, amax * fabsf(p.sc_pre) <= 0.5f)) {
+#pragma unroll
+          for (int c = 0; c < FWD_BN; ++c)
+            s[c] = __float_as_uint(tanh_small(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+        } else {
+#pragma unroll
+          for (int c = 0; c < FWD_BN; ++c)
+            s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+        }
         mul = 1.f;
       }
       const int c0 = j * FWD_BN;
