@@ -6,26 +6,32 @@
 // are bit-identical run to run):
 //   1. preprocess: Delta = rowsum(dO * O) and LSE in base-2 units, both padded
 //      to whole 128-row tiles (padding rows get LSE = +inf, so P = 0 there);
-//   2. dK/dV: one CTA per (batch, kv head, 128-key tile).  For every query
-//      head of the GQA group and every 128-row query tile that sees the keys:
+//   2. dK/dV: one CTA per (batch, kv head, 128-key tile).  It streams 64-row
+//      query sub-tiles of every query head of the GQA group that sees the keys:
 //        S^T = K Q^T, dP^T = V dO^T        (tensor cores, fp32 in TMEM)
 //        P^T = 2^(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - Delta) [* softcap']
 //        dV += P^T dO,  dK += dS^T Q      (P^T / dS^T as 16-bit A operands in TMEM)
-//   3. dQ: one CTA per (batch, query head, 128-row query tile):
-//        S = Q K^T, dP = dO V^T, dS as above, dQ += dS K.
+//   3. dQ: one CTA per (batch, query head, 128-row query tile), streaming
+//      64-key sub-tiles:  S = Q K^T, dP = dO V^T, dS as above, dQ += dS K.
+// Both main kernels double-buffer the score tiles in TMEM: two compute
+// warpgroups take alternate sub-tiles, so one computes P / dS while the tensor
+// core runs the other's accumulation MMAs and the next sub-tile's S and dP.
+//   warps 0-3 / 4-7  compute warpgroups 0 / 1 (one TMEM lane = one row each)
+//   warp 8           TMA producer
+//   warp 9           MMA issuer, TMEM owner
 // dK and dQ are multiplied by the softmax scale in their epilogues.
-// TMEM (dK/dV kernel): [0,128) S^T/P^T, [128,256) dP^T/dS^T, then dV, dK.
-// TMEM (dQ kernel):    [0,128) S/dS,    [128,256) dP,        then dQ.
+// TMEM (both kernels): buffer b at columns [128b, 128b+64) scores (S or S^T,
+// overwritten by 16-bit P^T / dS), [128b+64, 128b+128) dP; accumulators from 256.
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
 namespace ffa {
 
-constexpr int BWD_BM = 128;  // query rows per tile
-constexpr int BWD_BN = 128;  // keys per tile
-constexpr int BWD_THREADS = 192;  // warps 0-3 compute, 4 TMA producer, 5 MMA issuer + TMEM owner
-constexpr int BWD_WARP_LOAD = 4;
-constexpr int BWD_WARP_MMA = 5;
+constexpr int BWD_BT = 128;       // rows of the tile a CTA keeps (keys in dK/dV, queries in dQ)
+constexpr int BWD_BS = 64;        // rows of a streamed sub-tile
+constexpr int BWD_THREADS = 320;  // 2 compute warpgroups + TMA warp + MMA warp
+constexpr int BWD_WARP_LOAD = 8;
+constexpr int BWD_WARP_MMA = 9;
 
 struct BwdParams {
   // dK/dV kernel outputs
@@ -42,6 +48,7 @@ struct BwdParams {
   float scale;         // softmax scale (applied to dK / dQ in the epilogue)
   float scale_log2;
   float sc_pre, sc_post;
+  float sc_small;      // |raw score| below which tanh_small is accurate (0.5 / sc_pre)
   int use_softcap;
   int causal, window;
   ErrCtx ec;
@@ -56,81 +63,97 @@ enum : uint32_t {
   SITE_BWD_DRAIN = 0x206,
 };
 
-// Query-tile range [i_lo, i_hi) that interacts with key tile j.
+// 64-row query sub-tiles [i_lo, i_hi) that interact with 128-key tile j.
 __device__ __forceinline__ void q_range_for_key_tile(const BwdParams& p, int j, int& i_lo, int& i_hi) {
-  const int n_q = (p.Sq + BWD_BM - 1) / BWD_BM;
-  const int k_lo = j * BWD_BN, k_hi = min(k_lo + BWD_BN, p.Skv) - 1;
+  const int n_q = (p.Sq + BWD_BS - 1) / BWD_BS;
+  const int k_lo = j * BWD_BT, k_hi = min(k_lo + BWD_BT, p.Skv) - 1;
   i_lo = 0;
   i_hi = n_q;
   if (p.causal) {  // need some q_abs >= k_lo  ->  q >= k_lo - q_offset
     const int qmin = k_lo - p.q_offset;
-    i_lo = qmin > 0 ? qmin / BWD_BM : 0;
+    i_lo = qmin > 0 ? min(qmin / BWD_BS, n_q) : 0;
   }
   if (p.window > 0) {  // need some q_abs <= k_hi + window - 1
     const int qmax = k_hi + p.window - 1 - p.q_offset;
-    i_hi = qmax < 0 ? 0 : min(n_q, qmax / BWD_BM + 1);
+    i_hi = qmax < 0 ? 0 : min(n_q, qmax / BWD_BS + 1);
   }
   if (i_lo > i_hi) i_lo = i_hi;
 }
 
-// Key-tile range [j_lo, j_hi) that interacts with query tile i.
+// 64-key sub-tiles [j_lo, j_hi) that interact with 128-row query tile i.
 __device__ __forceinline__ void k_range_for_q_tile(const BwdParams& p, int i, int& j_lo, int& j_hi) {
-  const int n_kv = (p.Skv + BWD_BN - 1) / BWD_BN;
-  const int a_lo = i * BWD_BM + p.q_offset;
-  const int a_hi = min(i * BWD_BM + BWD_BM, p.Sq) - 1 + p.q_offset;
+  const int n_kv = (p.Skv + BWD_BS - 1) / BWD_BS;
+  const int a_lo = i * BWD_BT + p.q_offset;
+  const int a_hi = min(i * BWD_BT + BWD_BT, p.Sq) - 1 + p.q_offset;
   j_hi = n_kv;
-  if (p.causal) j_hi = min(n_kv, a_hi >= 0 ? a_hi / BWD_BN + 1 : 0);
+  if (p.causal) j_hi = min(n_kv, a_hi >= 0 ? a_hi / BWD_BS + 1 : 0);
   j_lo = 0;
   if (p.window > 0) {
     const int lo_col = a_lo - p.window + 1;
-    if (lo_col > 0) j_lo = min(lo_col / BWD_BN, j_hi);
+    if (lo_col > 0) j_lo = min(lo_col / BWD_BS, j_hi);
   }
 }
 
-__device__ __forceinline__ bool pair_visible(const BwdParams& p, int q_abs, int key) {
-  bool keep = key < p.Skv;
-  if (p.causal) keep = keep && key <= q_abs;
-  if (p.window > 0) keep = keep && key >= q_abs - p.window + 1;
-  return keep;
-}
-
-// P and dS for one 32-wide chunk of a TMEM row.  `s` holds raw Q.K scores,
-// `dp` holds dO.V values.  `lse2`/`delta` give the per-column (dK/dV kernel)
-// or per-row (dQ kernel, broadcast) statistics.
-template <typename T, bool COLS_ARE_QUERIES>
-__device__ __forceinline__ void bwd_chunk(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
-                                          const float* lse2_col, const float* delta_col, float lse2_row,
-                                          float delta_row, int row_pos, int col0, bool need_mask,
-                                          uint32_t* pk_p, uint32_t* pk_ds) {
+// P and dS for 32 columns of one TMEM row.  s: raw Q.K scores, dp: dO.V
+// values; l2 / dl: the base-2 LSE and Delta of each column (dK/dV kernel) or
+// of the row, broadcast (dQ kernel).  Columns c with (uint)(c - lo) >= cnt
+// are masked (lo = 0, cnt = 32 keeps all).
+// MODE 0: no softcap; 1: softcap through the series (FMA pipe); 2: softcap through ex2/rcp.
+template <typename T, bool WRITE_P, int MODE>
+__device__ __forceinline__ void bwd_chunk_body(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
+                                               const float* l2, const float* dl, int lo, uint32_t cnt,
+                                               uint32_t* pk_p, uint32_t* pk_ds) {
 #pragma unroll
-  for (int e = 0; e < 32; e += 2) {
+  for (int c = 0; c < 32; c += 2) {
     float pv[2], dv[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int c = e + u;
-      const float raw = __uint_as_float(s[c]);
+      const float raw = __uint_as_float(s[c + u]);
       float x, dsc = 1.f;
-      if (p.use_softcap) {
-        const float th = tanh_acc(raw * p.sc_pre);
-        x = th * p.sc_post;
-        dsc = 1.f - th * th;
-      } else {
+      if (MODE == 0) {
         x = raw * p.scale_log2;
+      } else {
+        const float th = MODE == 1 ? tanh_small(raw * p.sc_pre) : tanh_acc(raw * p.sc_pre);
+        x = th * p.sc_post;
+        dsc = fmaf(-th, th, 1.f);
       }
-      const float l2 = COLS_ARE_QUERIES ? lse2_col[c] : lse2_row;
-      const float dl = COLS_ARE_QUERIES ? delta_col[c] : delta_row;
-      float pr = ex2(x - l2);
-      if (need_mask) {
-        const int q_abs = COLS_ARE_QUERIES ? (col0 + c + p.q_offset) : row_pos;
-        const int key = COLS_ARE_QUERIES ? row_pos : (col0 + c);
-        if (!pair_visible(p, q_abs, key)) pr = 0.f;
-      }
+      float pr = ex2(x - l2[c + u]);
+      pr = ((uint32_t)(c + u - lo) < cnt) ? pr : 0.f;
       pv[u] = pr;
-      dv[u] = pr * (__uint_as_float(dp[c]) - dl) * dsc;
+      dv[u] = pr * (__uint_as_float(dp[c + u]) - dl[c + u]) * dsc;
     }
-    if (pk_p) pk_p[e / 2] = pack2<T>(pv[0], pv[1]);
-    pk_ds[e / 2] = pack2<T>(dv[0], dv[1]);
+    if (WRITE_P) pk_p[c / 2] = pack2<T>(pv[0], pv[1]);
+    pk_ds[c / 2] = pack2<T>(dv[0], dv[1]);
   }
+}
+
+template <typename T, bool WRITE_P>
+__device__ __forceinline__ void bwd_chunk(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
+                                          const float* l2, const float* dl, int lo, uint32_t cnt,
+                                          uint32_t* pk_p, uint32_t* pk_ds) {
+  if (!p.use_softcap) {
+    bwd_chunk_body<T, WRITE_P, 0>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+    return;
+  }
+  // The cap is usually far above the scores, so tanh's argument is small:
+  // then the series on the FMA pipe is exact to fp32 and spares the MUFU.
+  float mx = 0.f;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fabsf(__uint_as_float(s[c])));
+  if (__all_sync(0xffffffffu, mx <= p.sc_small))
+    bwd_chunk_body<T, WRITE_P, 1>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+  else
+    bwd_chunk_body<T, WRITE_P, 2>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+}
+
+// Columns [lo, lo + cnt) of a 32-wide chunk starting at column c0 that a row
+// keeps, from the row's kept range [r_lo, r_hi] (either end may lie outside
+// the chunk; cnt = 0 when the chunk keeps nothing).
+__device__ __forceinline__ void chunk_range(int r_lo, int r_hi, int c0, int& lo, uint32_t& cnt) {
+  const int a = max(r_lo - c0, 0);
+  const int z = min(r_hi - c0, 31);
+  lo = a;
+  cnt = z >= a ? (uint32_t)(z - a + 1) : 0u;
 }
 
 __device__ __forceinline__ float2 load2f(const __nv_bfloat16* p) {
@@ -138,6 +161,32 @@ __device__ __forceinline__ float2 load2f(const __nv_bfloat16* p) {
 }
 __device__ __forceinline__ float2 load2f(const __half* p) {
   return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Stores 32 fp32 accumulator columns of one row (times mul) as T.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const uint32_t* v, float mul, bool store) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) pk[e] = pack2<T>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
+  if (store) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+  }
+}
+
+// K-major smem descriptor offset of the ks-th 16-column K step in a tile of
+// `rows` rows stored as 64-column (128-byte) swizzled chunks.
+__device__ __forceinline__ uint64_t kstep(int ks, int rows) {
+  return (uint64_t)(((ks / 4) * rows * 128 + (ks % 4) * 32) >> 4);
 }
 
 // ---------------------------------------------------------------------------
@@ -177,37 +226,33 @@ __global__ void ffa_bwd_pre_kernel(const T* __restrict__ o, const T* __restrict_
   }
 }
 
+
 // ---------------------------------------------------------------------------
 // 2. dK / dV
 // ---------------------------------------------------------------------------
 template <int D>
 struct DkdvCfg {
-  static constexpr int TILE = 128 * D * 2;
+  static constexpr int TILE = BWD_BT * D * 2;  // K or V tile (128 rows)
+  static constexpr int SUB = BWD_BS * D * 2;   // Q or dO sub-tile (64 rows)
+  static constexpr int NS = D == 64 ? 8 : 4;   // stages of {Q, dO, stats}
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;                // 2 stages of {Q, dO}
-  static constexpr int STAT_OFF = STAGE_OFF + 4 * TILE;     // 2 stages of {lse2[128], delta[128]}
-  static constexpr int BAR_OFF = STAT_OFF + 2 * 2 * 128 * 4;
+  static constexpr int STAGE_OFF = 2 * TILE;          // stage s: Q at 2*s*SUB, dO at (2*s+1)*SUB
+  static constexpr int STAT_OFF = STAGE_OFF + NS * 2 * SUB;  // stage s: lse2[64], delta[64]
+  static constexpr int BAR_OFF = STAT_OFF + NS * 2 * BWD_BS * 4;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-struct DkdvBars {
-  uint64_t kv_full;
-  uint64_t st_full[2];
-  uint64_t st_empty[2];
-  uint64_t sp_full;
-  uint64_t ds_ready;
+struct BwdBars {
+  uint64_t fixed_full;    // the tile the CTA keeps (K/V or Q/dO)
+  uint64_t st_full[8];
+  uint64_t st_empty[8];
+  uint64_t sp_full[2];    // S and dP of buffer b computed
+  uint64_t ds_ready[2];   // P / dS of buffer b written back (128 arrivals)
   uint64_t acc_done;
   uint32_t tmem_base;
   int abort;
 };
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
@@ -215,34 +260,40 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                         const BwdParams p) {
   using Cfg = DkdvCfg<D>;
+  constexpr int NS = Cfg::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + Cfg::K_OFF;
   uint8_t* sV = smem + Cfg::V_OFF;
-  uint8_t* sStage = smem + Cfg::STAGE_OFF;  // stage s: Q at 2*s*TILE, dO at (2*s+1)*TILE
-  float* sStat = reinterpret_cast<float*>(smem + Cfg::STAT_OFF);  // stage s: lse2 at 256*s, delta at 256*s+128
-  DkdvBars* bars = reinterpret_cast<DkdvBars*>(smem + Cfg::BAR_OFF);
+  uint8_t* sStage = smem + Cfg::STAGE_OFF;
+  float* sStat = reinterpret_cast<float*>(smem + Cfg::STAT_OFF);
+  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::BAR_OFF);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int j = blockIdx.x;
-  const int bhk = blockIdx.y;
+  // Key-tile-major order: under causal masking the first key tiles see the
+  // most queries, so they are dispatched first.
+  const int BHk = p.B * p.Hkv;
+  const int j = blockIdx.x / BHk;
+  const int bhk = blockIdx.x % BHk;
   const int b = bhk / p.Hkv, hkv = bhk % p.Hkv;
   const int group = p.Hq / p.Hkv;
   int i_lo, i_hi;
   q_range_for_key_tile(p, j, i_lo, i_hi);
   const int n_i = i_hi - i_lo;
-  const int n_pairs = n_i * group;  // (query head of the group, query tile) pairs, head-major
+  const int n = n_i * group;  // units: (query head of the group, 64-row query sub-tile), head-major
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(&bars->fixed_full, 1);
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->st_full[s], 1);
       mbar_init(&bars->st_empty[s], 1);
     }
-    mbar_init(&bars->sp_full, 1);
-    mbar_init(&bars->ds_ready, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->sp_full[t], 1);
+      mbar_init(&bars->ds_ready[t], 128);
+    }
     mbar_init(&bars->acc_done, 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -257,152 +308,147 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == BWD_WARP_LOAD) {
-    if (lane == 0 && n_pairs > 0) {
+    if (lane == 0 && n > 0) {
       const uint64_t pol = policy_evict_last();
-      mbar_arrive_expect_tx(&bars->kv_full, 2 * Cfg::TILE);
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(&tmK, &bars->kv_full, sK + c * 128 * 128, c * 64, j * BWD_BN, hkv, b, pol);
-        tma_load_4d(&tmV, &bars->kv_full, sV + c * 128 * 128, c * 64, j * BWD_BN, hkv, b, pol);
-      }
-      int issued = 0;
-      for (int pi = 0; pi < n_pairs; ++pi) {
-        const int s = pi & 1, use = pi >> 1;
-        if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
-        const int g = pi / n_i, i = i_lo + pi % n_i;
-        const int h = hkv * group + g;
-        mbar_arrive_expect_tx(&bars->st_full[s], 2 * Cfg::TILE + 2 * 128 * 4);
-        uint8_t* dst = sStage + 2 * s * Cfg::TILE;
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(&tmQ, &bars->st_full[s], dst + c * 128 * 128, c * 64, i * BWD_BM, h, b, pol);
-          tma_load_4d(&tmDO, &bars->st_full[s], dst + Cfg::TILE + c * 128 * 128, c * 64, i * BWD_BM, h, b, pol);
+      mbar_arrive_expect_tx(&bars->fixed_full, 2 * Cfg::TILE);
+      for (int c = 0; c < D / 64; ++c)
+        for (int hf = 0; hf < 2; ++hf) {
+          const int off = c * BWD_BT * 128 + hf * BWD_BS * 128;
+          tma_load_4d(&tmK, &bars->fixed_full, sK + off, c * 64, j * BWD_BT + hf * BWD_BS, hkv, b, pol);
+          tma_load_4d(&tmV, &bars->fixed_full, sV + off, c * 64, j * BWD_BT + hf * BWD_BS, hkv, b, pol);
         }
-        const int64_t row0 = (int64_t)(b * p.Hq + h) * p.Sq_pad + i * BWD_BM;
-        bulk_load(sStat + 256 * s, p.lse2 + row0, 128 * 4, &bars->st_full[s]);
-        bulk_load(sStat + 256 * s + 128, p.delta + row0, 128 * 4, &bars->st_full[s]);
+      int issued = 0;
+      for (int u = 0; u < n; ++u) {
+        const int s = u % NS, use = u / NS;
+        if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
+        const int g = u / n_i, i = i_lo + u % n_i;
+        const int h = hkv * group + g;
+        mbar_arrive_expect_tx(&bars->st_full[s], 2 * Cfg::SUB + 2 * BWD_BS * 4);
+        uint8_t* dst = sStage + 2 * s * Cfg::SUB;
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(&tmQ, &bars->st_full[s], dst + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
+          tma_load_4d(&tmDO, &bars->st_full[s], dst + Cfg::SUB + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
+        }
+        const int64_t row0 = (int64_t)(b * p.Hq + h) * p.Sq_pad + i * BWD_BS;
+        bulk_load(sStat + 2 * BWD_BS * s, p.lse2 + row0, BWD_BS * 4, &bars->st_full[s]);
+        bulk_load(sStat + 2 * BWD_BS * s + BWD_BS, p.delta + row0, BWD_BS * 4, &bars->st_full[s]);
         ++issued;
       }
-      if (*abort_flag) {
-        mbar_wait(&bars->kv_full, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
-        for (int q = max(0, issued - 2); q < issued; ++q)
-          mbar_wait(&bars->st_full[q & 1], (q >> 1) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      if (*abort_flag) {  // let copies in flight land before the CTA exits
+        mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+        for (int u = max(0, issued - NS); u < issued; ++u)
+          mbar_wait(&bars->st_full[u % NS], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       }
     }
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
-    if (lane == 0 && n_pairs > 0) {
-      const uint32_t idesc_t = make_idesc_f16(128, 128, FMT, 0, 0);  // S^T, dP^T (K-major x K-major)
-      const uint32_t idesc_acc = make_idesc_f16(128, D, FMT, 0, 1);  // dV, dK (TMEM A x MN-major B)
+    if (lane == 0 && n > 0) {
+      const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (K-major x K-major)
+      const uint32_t idesc_acc = make_idesc_f16(128, D, FMT, 0, 1);     // dV, dK (TMEM A x MN-major B)
       const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
       const uint64_t v_desc = make_sdesc_sw128(smem_u32(sV), 16, 1024);
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
-      const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), 128 * 128, 1024);
-      const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
-      bool ok = mbar_wait(&bars->kv_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      for (int pi = 0; pi < n_pairs && ok; ++pi) {
-        const int s = pi & 1;
-        if (!(ok = mbar_wait(&bars->st_full[s], (pi >> 1) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
+      const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
+      const uint32_t tDV = tmem + 256, tDK = tmem + 256 + D;
+      // dV += P^T dO and dK += dS^T Q for unit v (after its compute group is done)
+      auto accumulate = [&](int v) -> bool {
+        const int bb = v & 1, s = v % NS;
+        if (!mbar_wait(&bars->ds_ready[bb], (v >> 1) & 1, p.ec, abort_flag, SITE_BWD_DS)) return false;
         tc_fence_after();
-        const uint64_t q_k = st_kdesc + (uint64_t)((2 * s * Cfg::TILE) >> 4);
-        const uint64_t do_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::TILE) >> 4);
+        const uint64_t q_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t do_m = st_mdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint32_t tP = tmem + 128 * bb, tDS = tP + 64;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = ((ks / 4) * (128 * 128) + (ks % 4) * 32) >> 4;
-          mma_ss(tS, k_desc + off, q_k + off, idesc_t, ks > 0);
-        }
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ts(tDV, tP + ks * 8, do_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc, (v > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = ((ks / 4) * (128 * 128) + (ks % 4) * 32) >> 4;
-          mma_ss(tDP, v_desc + off, do_k + off, idesc_t, ks > 0);
-        }
-        mma_commit(&bars->sp_full);
-        if (!(ok = mbar_wait(&bars->ds_ready, pi & 1, p.ec, abort_flag, SITE_BWD_DS))) break;
-        tc_fence_after();
-        const uint64_t q_m = st_mdesc + (uint64_t)((2 * s * Cfg::TILE) >> 4);
-        const uint64_t do_m = st_mdesc + (uint64_t)(((2 * s + 1) * Cfg::TILE) >> 4);
-#pragma unroll
-        for (int ks = 0; ks < BWD_BM / 16; ++ks) {
-          const uint32_t off = (ks * 16 * 128) >> 4;
-          mma_ts(tDV, tS + ks * 8, do_m + off, idesc_acc, (pi > 0 || ks > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int ks = 0; ks < BWD_BM / 16; ++ks) {
-          const uint32_t off = (ks * 16 * 128) >> 4;
-          mma_ts(tDK, tDP + ks * 8, q_m + off, idesc_acc, (pi > 0 || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ts(tDK, tDS + ks * 8, q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc, (v > 0 || ks > 0) ? 1u : 0u);
         mma_commit(&bars->st_empty[s]);
+        return true;
+      };
+      bool ok = mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+      for (int u = 0; u < n && ok; ++u) {
+        const int s = u % NS, bb = u & 1;
+        if (!(ok = mbar_wait(&bars->st_full[s], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
+        tc_fence_after();
+        const uint64_t q_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t do_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint32_t tS = tmem + 128 * bb, tDP = tS + 64;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) mma_ss(tS, k_desc + kstep(ks, BWD_BT), q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          mma_ss(tDP, v_desc + kstep(ks, BWD_BT), do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        mma_commit(&bars->sp_full[bb]);
+        if (u > 0 && !(ok = accumulate(u - 1))) break;
       }
+      if (ok) ok = accumulate(n - 1);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
     __syncwarp();
   } else {
     // ------------------------- compute (key rows) -------------------------
-    const int r = threadIdx.x;  // key row within the tile = TMEM lane
+    const int wg = warp / 4;
+    const int r = threadIdx.x % 128;  // key row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tDP = tmem + lane_off + 128;
-    const int key = j * BWD_BN + r;
+    const uint32_t tS = tmem + lane_off + 128 * wg, tDP = tS + 64;
+    const int key = j * BWD_BT + r;
+    // Kept query columns of this key, in absolute query positions minus q_offset:
+    // causal keeps q >= key - q_offset, the window keeps q <= key + window - 1 - q_offset.
+    const int q_keep_lo = p.causal ? key - p.q_offset : -0x3fffffff;
+    const int q_keep_hi = key >= p.Skv ? -0x40000000 : (p.window > 0 ? key + p.window - 1 - p.q_offset : 0x3fffffff);
     bool ok = true;
-    for (int pi = 0; pi < n_pairs; ++pi) {
-      const int s = pi & 1;
-      const int i = i_lo + pi % n_i;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full, pi & 1, p.ec, abort_flag, SITE_BWD_SP));
+    for (int u = wg; u < n; u += 2) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[wg], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
       if (!ok) break;
       tc_fence_after();
-      const int q0 = i * BWD_BM;
-      // masks are needed where the tile straddles a causal / window / length edge
-      const int qa_lo = q0 + p.q_offset, qa_hi = q0 + BWD_BM - 1 + p.q_offset;
-      const int k_lo = j * BWD_BN, k_hi = k_lo + BWD_BN - 1;
-      const bool need_mask = (p.causal && k_hi > qa_lo) || (p.window > 0 && k_lo < qa_hi - p.window + 1) ||
-                             (k_hi >= p.Skv);
-      const float* lse2 = sStat + 256 * s;
-      const float* delta = lse2 + 128;
-#pragma unroll 1
-      for (int cb = 0; cb < BWD_BM; cb += 32) {
+      const int s = u % NS;
+      const int q0 = (i_lo + u % n_i) * BWD_BS;
+      const float* l2 = sStat + 2 * BWD_BS * s;
+      const float* dl = l2 + BWD_BS;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
         uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + cb, sv);
-        tmem_ld32(tDP + cb, dpv);
+        tmem_ld32(tS + hf * 32, sv);
+        tmem_ld32(tDP + hf * 32, dpv);
         tmem_ld_wait32(sv);
         tmem_ld_wait32(dpv);
+        int lo;
+        uint32_t cnt;
+        chunk_range(q_keep_lo, q_keep_hi, q0 + hf * 32, lo, cnt);
         uint32_t pk_p[16], pk_ds[16];
-        bwd_chunk<T, true>(p, sv, dpv, lse2 + cb, delta + cb, 0.f, 0.f, key, q0 + cb, need_mask, pk_p, pk_ds);
-        tmem_st16(tS + cb / 2, pk_p);
-        tmem_st16(tDP + cb / 2, pk_ds);
+        bwd_chunk<T, true>(p, sv, dpv, l2 + hf * 32, dl + hf * 32, lo, cnt, pk_p, pk_ds);
+        tmem_st16(tS + hf * 16, pk_p);
+        tmem_st16(tDP + hf * 16, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->ds_ready);
+      mbar_arrive(&bars->ds_ready[wg]);
     }
     // ------------------------------ epilogue ------------------------------
-    const bool have = ok && n_pairs > 0 &&
+    // warpgroup 0 stores dV, warpgroup 1 stores dK (times the softmax scale)
+    const bool have = ok && n > 0 &&
                       __all_sync(0xffffffffu, mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DONE));
     if (have) tc_fence_after();
     const bool store = key < p.Skv;
-    T* dvrow = reinterpret_cast<T*>(p.dv) + (size_t)b * p.dv_sb + (size_t)hkv * p.dv_sh + (size_t)key * p.dv_ss;
-    T* dkrow = reinterpret_cast<T*>(p.dk) + (size_t)b * p.dk_sb + (size_t)hkv * p.dk_sh + (size_t)key * p.dk_ss;
+    T* row = wg == 0
+                 ? reinterpret_cast<T*>(p.dv) + (size_t)b * p.dv_sb + (size_t)hkv * p.dv_sh + (size_t)key * p.dv_ss
+                 : reinterpret_cast<T*>(p.dk) + (size_t)b * p.dk_sb + (size_t)hkv * p.dk_sh + (size_t)key * p.dk_ss;
+    const uint32_t tacc = tmem + lane_off + 256 + wg * D;
+    const float mul = wg ? p.scale : 1.f;
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const uint32_t tacc = tmem + lane_off + 256 + which * D;
-      const float mul = which ? p.scale : 1.f;
-      T* dst_row = which ? dkrow : dvrow;
+    for (int c = 0; c < D; c += 32) {
+      uint32_t v[32];
+      if (have) {
+        tmem_ld32(tacc + c, v);
+        tmem_ld_wait32(v);
+      } else {
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t v[32];
-        if (have) {
-          tmem_ld32(tacc + c, v);
-          tmem_ld_wait32(v);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = 0u;
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack2<T>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
-        if (store) {
-          uint4* dst = reinterpret_cast<uint4*>(dst_row + c);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-        }
+        for (int e = 0; e < 32; ++e) v[e] = 0u;
       }
+      store_row32<T>(row + c, v, mul, store);
     }
   }
   tc_fence_before();
@@ -418,23 +464,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // ---------------------------------------------------------------------------
 template <int D>
 struct DqCfg {
-  static constexpr int TILE = 128 * D * 2;
+  static constexpr int TILE = BWD_BT * D * 2;  // Q or dO tile (128 rows)
+  static constexpr int SUB = BWD_BS * D * 2;   // K or V sub-tile (64 rows)
+  static constexpr int NS = D == 64 ? 8 : 4;   // stages of {K, V}
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = TILE;
-  static constexpr int KV_OFF = 2 * TILE;  // 2 stages of {K, V}
-  static constexpr int BAR_OFF = KV_OFF + 4 * TILE;
+  static constexpr int STAGE_OFF = 2 * TILE;  // stage s: K at 2*s*SUB, V at (2*s+1)*SUB
+  static constexpr int BAR_OFF = STAGE_OFF + NS * 2 * SUB;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
-};
-
-struct DqBars {
-  uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
-  uint64_t sp_full;
-  uint64_t ds_ready;
-  uint64_t acc_done;
-  uint32_t tmem_base;
-  int abort;
 };
 
 template <typename T, int D>
@@ -443,34 +480,39 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                       const BwdParams p) {
   using Cfg = DqCfg<D>;
+  constexpr int NS = Cfg::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
   uint8_t* sDO = smem + Cfg::DO_OFF;
-  uint8_t* sKV = smem + Cfg::KV_OFF;  // stage s: K at 2*s*TILE, V at (2*s+1)*TILE
-  DqBars* bars = reinterpret_cast<DqBars*>(smem + Cfg::BAR_OFF);
+  uint8_t* sStage = smem + Cfg::STAGE_OFF;
+  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::BAR_OFF);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int n_q = (p.Sq + BWD_BM - 1) / BWD_BM;
-  // heavier (later) query tiles first under causal masking
-  const int i = p.causal ? (n_q - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int bh = blockIdx.y;
+  const int n_q = (p.Sq + BWD_BT - 1) / BWD_BT;
+  // Query-tile-major order, heaviest (latest, under causal masking) first.
+  const int BH = p.B * p.Hq;
+  const int ii = blockIdx.x / BH;
+  const int i = p.causal ? (n_q - 1 - ii) : ii;
+  const int bh = blockIdx.x % BH;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int hkv = h / (p.Hq / p.Hkv);
   int j_lo, j_hi;
   k_range_for_q_tile(p, i, j_lo, j_hi);
-  const int n = max(0, j_hi - j_lo);
+  const int n = max(0, j_hi - j_lo);  // units: 64-key sub-tiles
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+    mbar_init(&bars->fixed_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars->st_full[s], 1);
+      mbar_init(&bars->st_empty[s], 1);
     }
-    mbar_init(&bars->sp_full, 1);
-    mbar_init(&bars->ds_ready, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->sp_full[t], 1);
+      mbar_init(&bars->ds_ready[t], 128);
+    }
     mbar_init(&bars->acc_done, 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -488,113 +530,129 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     if (lane == 0 && n > 0) {
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_last();
-      mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::TILE);
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(&tmQ, &bars->q_full, sQ + c * 128 * 128, c * 64, i * BWD_BM, h, b, pol_q);
-        tma_load_4d(&tmDO, &bars->q_full, sDO + c * 128 * 128, c * 64, i * BWD_BM, h, b, pol_q);
-      }
+      mbar_arrive_expect_tx(&bars->fixed_full, 2 * Cfg::TILE);
+      for (int c = 0; c < D / 64; ++c)
+        for (int hf = 0; hf < 2; ++hf) {
+          const int off = c * BWD_BT * 128 + hf * BWD_BS * 128;
+          tma_load_4d(&tmQ, &bars->fixed_full, sQ + off, c * 64, i * BWD_BT + hf * BWD_BS, h, b, pol_q);
+          tma_load_4d(&tmDO, &bars->fixed_full, sDO + off, c * 64, i * BWD_BT + hf * BWD_BS, h, b, pol_q);
+        }
       int issued = 0;
-      for (int it = 0; it < n; ++it) {
-        const int s = it & 1, use = it >> 1;
-        if (use > 0 && !mbar_wait(&bars->kv_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
-        const int j = j_lo + it;
-        mbar_arrive_expect_tx(&bars->kv_full[s], 2 * Cfg::TILE);
-        uint8_t* dst = sKV + 2 * s * Cfg::TILE;
+      for (int u = 0; u < n; ++u) {
+        const int s = u % NS, use = u / NS;
+        if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
+        const int jj = j_lo + u;
+        mbar_arrive_expect_tx(&bars->st_full[s], 2 * Cfg::SUB);
+        uint8_t* dst = sStage + 2 * s * Cfg::SUB;
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(&tmK, &bars->kv_full[s], dst + c * 128 * 128, c * 64, j * BWD_BN, hkv, b, pol_kv);
-          tma_load_4d(&tmV, &bars->kv_full[s], dst + Cfg::TILE + c * 128 * 128, c * 64, j * BWD_BN, hkv, b, pol_kv);
+          tma_load_4d(&tmK, &bars->st_full[s], dst + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b, pol_kv);
+          tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b, pol_kv);
         }
         ++issued;
       }
       if (*abort_flag) {
-        mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
-        for (int q = max(0, issued - 2); q < issued; ++q)
-          mbar_wait(&bars->kv_full[q & 1], (q >> 1) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+        mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+        for (int u = max(0, issued - NS); u < issued; ++u)
+          mbar_wait(&bars->st_full[u % NS], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       }
     }
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_s = make_idesc_f16(128, 128, FMT, 0, 0);
-      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);
+      const uint32_t idesc_s = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S, dP (K-major x K-major)
+      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);     // dQ (TMEM A x MN-major B)
       const uint64_t q_desc = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t do_desc = make_sdesc_sw128(smem_u32(sDO), 16, 1024);
-      const uint64_t kv_kdesc = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
-      const uint64_t kv_mdesc = make_sdesc_sw128(smem_u32(sKV), 128 * 128, 1024);
-      const uint32_t tS = tmem, tDP = tmem + 128, tDQ = tmem + 256;
-      bool ok = mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      for (int it = 0; it < n && ok; ++it) {
-        const int s = it & 1;
-        if (!(ok = mbar_wait(&bars->kv_full[s], (it >> 1) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
+      const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
+      const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
+      const uint32_t tDQ = tmem + 256;
+      auto accumulate = [&](int v) -> bool {
+        const int bb = v & 1, s = v % NS;
+        if (!mbar_wait(&bars->ds_ready[bb], (v >> 1) & 1, p.ec, abort_flag, SITE_BWD_DS)) return false;
         tc_fence_after();
-        const uint64_t k_k = kv_kdesc + (uint64_t)((2 * s * Cfg::TILE) >> 4);
-        const uint64_t v_k = kv_kdesc + (uint64_t)(((2 * s + 1) * Cfg::TILE) >> 4);
+        const uint64_t k_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint32_t tDS = tmem + 128 * bb;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = ((ks / 4) * (128 * 128) + (ks % 4) * 32) >> 4;
-          mma_ss(tS, q_desc + off, k_k + off, idesc_s, ks > 0);
-        }
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = ((ks / 4) * (128 * 128) + (ks % 4) * 32) >> 4;
-          mma_ss(tDP, do_desc + off, v_k + off, idesc_s, ks > 0);
-        }
-        mma_commit(&bars->sp_full);
-        if (!(ok = mbar_wait(&bars->ds_ready, it & 1, p.ec, abort_flag, SITE_BWD_DS))) break;
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ts(tDQ, tDS + ks * 8, k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq, (v > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(&bars->st_empty[s]);
+        return true;
+      };
+      bool ok = mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+      for (int u = 0; u < n && ok; ++u) {
+        const int s = u % NS, bb = u & 1;
+        if (!(ok = mbar_wait(&bars->st_full[s], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
         tc_fence_after();
-        const uint64_t k_m = kv_mdesc + (uint64_t)((2 * s * Cfg::TILE) >> 4);
+        const uint64_t k_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t v_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint32_t tS = tmem + 128 * bb, tDP = tS + 64;
 #pragma unroll
-        for (int ks = 0; ks < BWD_BN / 16; ++ks)
-          mma_ts(tDQ, tS + ks * 8, k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq, (it > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(&bars->kv_empty[s]);
+        for (int ks = 0; ks < D / 16; ++ks)
+          mma_ss(tS, q_desc + kstep(ks, BWD_BT), k_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          mma_ss(tDP, do_desc + kstep(ks, BWD_BT), v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+        mma_commit(&bars->sp_full[bb]);
+        if (u > 0 && !(ok = accumulate(u - 1))) break;
       }
+      if (ok) ok = accumulate(n - 1);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
     __syncwarp();
   } else {
     // ------------------------- compute (query rows) -----------------------
-    const int r = threadIdx.x;
+    const int wg = warp / 4;
+    const int r = threadIdx.x % 128;
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tDP = tmem + lane_off + 128;
-    const int row = i * BWD_BM + r;
+    const uint32_t tS = tmem + lane_off + 128 * wg, tDP = tS + 64;
+    const int row = i * BWD_BT + r;
     const int q_abs = row + p.q_offset;
     const int64_t sidx = (int64_t)(b * p.Hq + h) * p.Sq_pad + row;
-    const float lse2_r = p.lse2[sidx];
-    const float delta_r = p.delta[sidx];
-    const int a_lo = i * BWD_BM + p.q_offset, a_hi = min(i * BWD_BM + BWD_BM, p.Sq) - 1 + p.q_offset;
+    float l2c[32], dlc[32];
+    {
+      const float l = p.lse2[sidx], d = p.delta[sidx];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        l2c[c] = l;
+        dlc[c] = d;
+      }
+    }
+    // kept keys of this row: [q_abs - window + 1, min(q_abs, Skv - 1)]
+    const int k_keep_lo = p.window > 0 ? q_abs - p.window + 1 : -0x3fffffff;
+    const int k_keep_hi = min(p.causal ? q_abs : 0x3fffffff, p.Skv - 1);
     bool ok = true;
-    for (int it = 0; it < n; ++it) {
-      const int j = j_lo + it;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full, it & 1, p.ec, abort_flag, SITE_BWD_SP));
+    for (int u = wg; u < n; u += 2) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[wg], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
       if (!ok) break;
       tc_fence_after();
-      const int c0 = j * BWD_BN;
-      const bool need_mask = (p.causal && c0 + BWD_BN - 1 > a_lo) || (p.window > 0 && c0 < a_hi - p.window + 1) ||
-                             (c0 + BWD_BN > p.Skv);
-#pragma unroll 1
-      for (int cb = 0; cb < BWD_BN; cb += 32) {
+      const int c0 = (j_lo + u) * BWD_BS;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
         uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + cb, sv);
-        tmem_ld32(tDP + cb, dpv);
+        tmem_ld32(tS + hf * 32, sv);
+        tmem_ld32(tDP + hf * 32, dpv);
         tmem_ld_wait32(sv);
         tmem_ld_wait32(dpv);
+        int lo;
+        uint32_t cnt;
+        chunk_range(k_keep_lo, k_keep_hi, c0 + hf * 32, lo, cnt);
         uint32_t pk_ds[16];
-        bwd_chunk<T, false>(p, sv, dpv, nullptr, nullptr, lse2_r, delta_r, q_abs, c0 + cb, need_mask, nullptr,
-                            pk_ds);
-        tmem_st16(tS + cb / 2, pk_ds);
+        bwd_chunk<T, false>(p, sv, dpv, l2c, dlc, lo, cnt, nullptr, pk_ds);
+        tmem_st16(tS + hf * 16, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->ds_ready);
+      mbar_arrive(&bars->ds_ready[wg]);
     }
+    // epilogue: warpgroup 0 stores dQ columns [0, D/2), warpgroup 1 the rest
     const bool have = ok && n > 0 &&
                       __all_sync(0xffffffffu, mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DONE));
     if (have) tc_fence_after();
     const bool store = row < p.Sq;
     T* dqrow = reinterpret_cast<T*>(p.dq) + (size_t)b * p.dq_sb + (size_t)h * p.dq_sh + (size_t)row * p.dq_ss;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = wg * (D / 2); c < (wg + 1) * (D / 2); c += 32) {
       uint32_t v[32];
       if (have) {
         tmem_ld32(tmem + lane_off + 256 + c, v);
@@ -603,15 +661,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0u;
       }
-      uint32_t pk[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        pk[e] = pack2<T>(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale);
-      if (store) {
-        uint4* dst = reinterpret_cast<uint4*>(dqrow + c);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-      }
+      store_row32<T>(dqrow + c, v, p.scale, store);
     }
   }
   tc_fence_before();
@@ -648,7 +698,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
       if ((s = set_smem(kern, DkdvCfg<D>::SMEM))) return s;
       set = true;
     }
-    dim3 grid((p.Skv + BWD_BN - 1) / BWD_BN, p.B * p.Hkv);
+    const int grid = (p.Skv + BWD_BT - 1) / BWD_BT * p.B * p.Hkv;
     kern<<<grid, BWD_THREADS, DkdvCfg<D>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;
   }
@@ -660,7 +710,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
       if ((s = set_smem(kern, DqCfg<D>::SMEM))) return s;
       set = true;
     }
-    dim3 grid((p.Sq + BWD_BM - 1) / BWD_BM, p.B * p.Hq);
+    const int grid = (p.Sq + BWD_BT - 1) / BWD_BT * p.B * p.Hq;
     kern<<<grid, BWD_THREADS, DqCfg<D>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;
   }
@@ -728,6 +778,7 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
   p.use_softcap = softcap > 0.f;
   p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
   p.sc_post = p.use_softcap ? softcap * 1.4426950408889634f : 0.f;
+  p.sc_small = p.use_softcap ? 0.5f * softcap / scale : 0.f;
   p.causal = causal;
   p.window = window > 0 ? window : 0;
   p.ec.err = dev_err;
@@ -737,16 +788,16 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
       dtype == FFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap maps[4];
   int st = make_tmap_4d(&maps[0], q, dt, 2, D, Sq, Hq, B, q_strides[2] * 2, q_strides[1] * 2, q_strides[0] * 2, 64,
-                        BWD_BM);
+                        BWD_BS);
   if (!st)
     st = make_tmap_4d(&maps[1], k, dt, 2, D, Skv, Hkv, B, k_strides[2] * 2, k_strides[1] * 2, k_strides[0] * 2, 64,
-                      BWD_BN);
+                      BWD_BS);
   if (!st)
     st = make_tmap_4d(&maps[2], v, dt, 2, D, Skv, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
-                      BWD_BN);
+                      BWD_BS);
   if (!st)
     st = make_tmap_4d(&maps[3], dout, dt, 2, D, Sq, Hq, B, do_strides[2] * 2, do_strides[1] * 2, do_strides[0] * 2,
-                      64, BWD_BM);
+                      64, BWD_BS);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FFA_DTYPE_BF16) {
