@@ -4,24 +4,31 @@
 // kernels/cpu_fa4.py:445 fa4_backward and kernels/triton_bwd.py behind
 // ffa_bwd().  Three launches, no atomics, fixed summation order (so results
 // are bit-identical run to run):
-//   1. preprocess: Delta = rowsum(dO * O) and LSE in base-2 units, both padded
-//      to whole 128-row tiles (padding rows get LSE = +inf, so P = 0 there);
+//   1. preprocess: Delta = rowsum(dO * O) and NLSE2 = -LSE in base-2 units,
+//      both padded to whole 128-row tiles (padding rows get NLSE2 = -inf, so
+//      P = 0 there);
 //   2. dK/dV: one CTA per (batch, kv head, 128-key tile).  It streams 64-row
 //      query sub-tiles of every query head of the GQA group that sees the keys:
 //        S^T = K Q^T, dP^T = V dO^T        (tensor cores, fp32 in TMEM)
-//        P^T = 2^(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - Delta) [* softcap']
+//        P^T = 2^(S^T*scale*log2e + NLSE2), dS^T = P^T (dP^T - Delta) [* softcap']
 //        dV += P^T dO,  dK += dS^T Q      (P^T / dS^T as 16-bit A operands in TMEM)
 //   3. dQ: one CTA per (batch, query head, 128-row query tile), streaming
 //      64-key sub-tiles:  S = Q K^T, dP = dO V^T, dS as above, dQ += dS K.
-// Both main kernels double-buffer the score tiles in TMEM: two compute
-// warpgroups take alternate sub-tiles, so one computes P / dS while the tensor
-// core runs the other's accumulation MMAs and the next sub-tile's S and dP.
-//   warps 0-3 / 4-7  compute warpgroups 0 / 1 (one TMEM lane = one row each)
-//   warp 8           TMA producer
-//   warp 9           MMA issuer, TMEM owner
+// Both main kernels double-buffer the score tiles in TMEM: alternate sub-tiles
+// go to alternate buffers.  A compute warpgroup loads its S / dP columns into
+// registers and releases the TMEM buffer at once, then writes the 16-bit P^T /
+// dS tiles to shared memory (128-byte swizzled, K-major: the A operands of the
+// accumulation MMAs).  So the next S / dP MMAs into a buffer never wait for
+// the accumulation MMAs of the sub-tile before, and the tensor core runs
+// S(u+1), dV/dK(u) while unit u+1's compute overlaps them.
+//   warps 0-15  compute warpgroups 0-3: warpgroup w serves buffer w % 2 and
+//               columns [32 (w / 2), 32 (w / 2) + 32) of its 64-column
+//               sub-tile; one TMEM lane = one row
+//   warp 16     TMA producer
+//   warp 17     MMA issuer, TMEM owner
 // dK and dQ are multiplied by the softmax scale in their epilogues.
-// TMEM (both kernels): buffer b at columns [128b, 128b+64) scores (S or S^T,
-// overwritten by 16-bit P^T / dS), [128b+64, 128b+128) dP; accumulators from 256.
+// TMEM (both kernels): buffer b at columns [128b, 128b+64) scores (S or S^T),
+// [128b+64, 128b+128) dP; accumulators from 256.
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
@@ -29,9 +36,10 @@ namespace ffa {
 
 constexpr int BWD_BT = 128;       // rows of the tile a CTA keeps (keys in dK/dV, queries in dQ)
 constexpr int BWD_BS = 64;        // rows of a streamed sub-tile
-constexpr int BWD_THREADS = 320;  // 2 compute warpgroups + TMA warp + MMA warp
-constexpr int BWD_WARP_LOAD = 8;
-constexpr int BWD_WARP_MMA = 9;
+constexpr int BWD_NWG = 4;         // compute warpgroups: two per TMEM buffer, 32 columns each
+constexpr int BWD_THREADS = BWD_NWG * 128 + 64;  // + TMA warp + MMA warp
+constexpr int BWD_WARP_LOAD = BWD_NWG * 4;
+constexpr int BWD_WARP_MMA = BWD_NWG * 4 + 1;
 
 struct BwdParams {
   // dK/dV kernel outputs
@@ -41,7 +49,7 @@ struct BwdParams {
   // dQ kernel output
   void* dq;
   int64_t dq_sb, dq_sh, dq_ss;
-  const float* lse2;   // [B*Hq, Sq_pad] base-2 LSE, +inf on padding rows
+  const float* nlse2;  // [B*Hq, Sq_pad] minus the base-2 LSE, -inf on padding rows
   const float* delta;  // [B*Hq, Sq_pad]
   int Sq_pad;
   int B, Hq, Hkv, Sq, Skv, q_offset;
@@ -94,66 +102,148 @@ __device__ __forceinline__ void k_range_for_q_tile(const BwdParams& p, int i, in
   }
 }
 
-// P and dS for 32 columns of one TMEM row.  s: raw Q.K scores, dp: dO.V
-// values; l2 / dl: the base-2 LSE and Delta of each column (dK/dV kernel) or
-// of the row, broadcast (dQ kernel).  Columns c with (uint)(c - lo) >= cnt
-// are masked (lo = 0, cnt = 32 keeps all).
-// MODE 0: no softcap; 1: softcap through the series (FMA pipe); 2: softcap through ex2/rcp.
-template <typename T, bool WRITE_P, int MODE>
-__device__ __forceinline__ void bwd_chunk_body(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
-                                               const float* l2, const float* dl, int lo, uint32_t cnt,
-                                               uint32_t* pk_p, uint32_t* pk_ds) {
+// P and dS for 16 columns of one TMEM row.  s: raw Q.K scores, dp: dO.V
+// values.  Minus the base-2 LSE and Delta of each column come from smem
+// (COL_STATS, dK/dV kernel: cnl2 / cdl, 16-byte aligned) or are the row's
+// (rnl2 / rdl, dQ kernel).  With MASKED, columns c with (uint)(c - lo) >= cnt
+// are dropped.  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
+// pipe); 2: softcap with tanh through ex2 / rcp.
+template <typename T, bool WRITE_P, bool COL_STATS, int MODE, bool MASKED>
+__device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
+                                            const float* cnl2, const float* cdl, float rnl2, float rdl, int lo,
+                                            uint32_t cnt, uint32_t* pk_p, uint32_t* pk_ds) {
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    float pv[2], dv[2];
+  for (int c4 = 0; c4 < 16; c4 += 4) {
+    float nl2[4], dl[4];
+    if (COL_STATS) {
+      const float4 a = *reinterpret_cast<const float4*>(cnl2 + c4);
+      const float4 z = *reinterpret_cast<const float4*>(cdl + c4);
+      nl2[0] = a.x; nl2[1] = a.y; nl2[2] = a.z; nl2[3] = a.w;
+      dl[0] = z.x; dl[1] = z.y; dl[2] = z.z; dl[3] = z.w;
+    } else {
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float raw = __uint_as_float(s[c + u]);
-      float x, dsc = 1.f;
-      if (MODE == 0) {
-        x = raw * p.scale_log2;
-      } else {
-        const float th = MODE == 1 ? tanh_small(raw * p.sc_pre) : tanh_acc(raw * p.sc_pre);
-        x = th * p.sc_post;
-        dsc = fmaf(-th, th, 1.f);
+      for (int e = 0; e < 4; ++e) {
+        nl2[e] = rnl2;
+        dl[e] = rdl;
       }
-      float pr = ex2(x - l2[c + u]);
-      pr = ((uint32_t)(c + u - lo) < cnt) ? pr : 0.f;
-      pv[u] = pr;
-      dv[u] = pr * (__uint_as_float(dp[c + u]) - dl[c + u]) * dsc;
     }
-    if (WRITE_P) pk_p[c / 2] = pack2<T>(pv[0], pv[1]);
-    pk_ds[c / 2] = pack2<T>(dv[0], dv[1]);
+#pragma unroll
+    for (int c2 = 0; c2 < 4; c2 += 2) {
+      float pv[2], dv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = c4 + c2 + u;
+        const float raw = __uint_as_float(s[c]);
+        float pr, g;
+        if (MODE == 0) {
+          pr = ex2(fmaf(raw, p.scale_log2, nl2[c2 + u]));
+          g = __uint_as_float(dp[c]) - dl[c2 + u];
+        } else {
+          const float th = MODE == 1 ? tanh_small(raw * p.sc_pre) : tanh_acc(raw * p.sc_pre);
+          pr = ex2(fmaf(th, p.sc_post, nl2[c2 + u]));
+          g = (__uint_as_float(dp[c]) - dl[c2 + u]) * fmaf(-th, th, 1.f);
+        }
+        if (MASKED) pr = ((uint32_t)(c - lo) < cnt) ? pr : 0.f;
+        pv[u] = pr;
+        dv[u] = pr * g;
+      }
+      if (WRITE_P) pk_p[(c4 + c2) / 2] = pack2<T>(pv[0], pv[1]);
+      pk_ds[(c4 + c2) / 2] = pack2<T>(dv[0], dv[1]);
+    }
   }
 }
 
-template <typename T, bool WRITE_P>
-__device__ __forceinline__ void bwd_chunk(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
-                                          const float* l2, const float* dl, int lo, uint32_t cnt,
-                                          uint32_t* pk_p, uint32_t* pk_ds) {
+template <typename T, bool WRITE_P, bool COL_STATS, bool MASKED>
+__device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
+                                                 const float* cnl2, const float* cdl, float rnl2, float rdl,
+                                                 int lo, uint32_t cnt, uint32_t* pk_p, uint32_t* pk_ds) {
   if (!p.use_softcap) {
-    bwd_chunk_body<T, WRITE_P, 0>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 0, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
     return;
   }
   // The cap is usually far above the scores, so tanh's argument is small:
   // then the series on the FMA pipe is exact to fp32 and spares the MUFU.
   float mx = 0.f;
 #pragma unroll
-  for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fabsf(__uint_as_float(s[c])));
+  for (int c = 0; c < 16; c += 2) mx = fmax3(mx, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
   if (__all_sync(0xffffffffu, mx <= p.sc_small))
-    bwd_chunk_body<T, WRITE_P, 1>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 1, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
   else
-    bwd_chunk_body<T, WRITE_P, 2>(p, s, dp, l2, dl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 2, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
 }
 
-// Columns [lo, lo + cnt) of a 32-wide chunk starting at column c0 that a row
-// keeps, from the row's kept range [r_lo, r_hi] (either end may lie outside
-// the chunk; cnt = 0 when the chunk keeps nothing).
-__device__ __forceinline__ void chunk_range(int r_lo, int r_hi, int c0, int& lo, uint32_t& cnt) {
-  const int a = max(r_lo - c0, 0);
-  const int z = min(r_hi - c0, 31);
-  lo = a;
-  cnt = z >= a ? (uint32_t)(z - a + 1) : 0u;
+// Stores 16-byte chunk `chunk` of row `row` of a 128-byte-swizzled K-major
+// tile (the layout TMA's SWIZZLE_128B writes and the MMA descriptors read):
+// chunk j of row r sits at r * 128 + 16 * (j ^ (r % 8)).  Rows 0-7 of the
+// eight threads that store one chunk fall into distinct bank groups.
+__device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, uint32_t a, uint32_t b, uint32_t c,
+                                         uint32_t d) {
+  *reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4)) = make_uint4(a, b, c, d);
+}
+
+// P / dS for this thread's 32 columns of a unit (one TMEM row = tile row
+// `row`).  tS / tDP address the first of the 32 columns; the TMEM buffer is
+// released (arrive on `tmem_free`) as soon as the values are in registers.
+// Column statistics come from smem (COL_STATS: cnl2 / cdl for the first
+// column) or are the row's (rnl2, rdl).  The row keeps columns
+// [keep_lo, keep_hi] of the 32; `masked` (warp-uniform) is false when no row
+// of the warp drops any column.  Before storing, waits (if pt_parity >= 0)
+// for `pt_free` to show that the smem tiles' previous contents were consumed;
+// then P^T (WRITE_P) goes to sP and dS to sDS, as 16-byte chunks
+// 4*half .. 4*half+3 of the row.  Returns false if that wait gave up.
+template <typename T, bool WRITE_P, bool COL_STATS>
+__device__ __forceinline__ bool bwd_unit(const BwdParams& p, uint32_t tS, uint32_t tDP, uint64_t* tmem_free,
+                                         const float* cnl2, const float* cdl, float rnl2, float rdl, int keep_lo,
+                                         int keep_hi, bool masked, uint64_t* pt_free, int pt_parity,
+                                         volatile int* abort_flag, uint8_t* sP, uint8_t* sDS, int row, int half) {
+  uint32_t s[32], d[32];
+  tmem_ld32(tS, s);
+  tmem_ld32(tDP, d);
+  tmem_ld_wait32(s);
+  tmem_ld_wait32(d);
+  tc_fence_before();
+  __syncwarp();
+  if (lane_id() == 0) mbar_arrive(tmem_free);
+  uint32_t pp[16], pd[16];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float* n2 = COL_STATS ? cnl2 + 16 * k : nullptr;
+    const float* d2 = COL_STATS ? cdl + 16 * k : nullptr;
+    if (masked) {
+      const int lo = max(keep_lo - 16 * k, 0);
+      const int z = min(keep_hi - 16 * k, 15);
+      const uint32_t cnt = z >= lo ? (uint32_t)(z - lo + 1) : 0u;
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, true>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, lo, cnt,
+                                                    pp + 8 * k, pd + 8 * k);
+    } else {
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, false>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, 0, 16u,
+                                                     pp + 8 * k, pd + 8 * k);
+    }
+  }
+  if (pt_parity >= 0 &&
+      !__all_sync(0xffffffffu, mbar_wait(pt_free, (uint32_t)pt_parity, p.ec, abort_flag, SITE_BWD_EMPTY)))
+    return false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (WRITE_P) st_sw128(sP, row, 4 * half + q, pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
+    st_sw128(sDS, row, 4 * half + q, pd[4 * q], pd[4 * q + 1], pd[4 * q + 2], pd[4 * q + 3]);
+  }
+  fence_async_smem();  // the generic-proxy stores -> visible to the tensor core
+  __syncwarp();
+  return true;
+}
+
+// Stores 16 fp32 accumulator columns of one row (times mul) as T.
+template <typename T>
+__device__ __forceinline__ void store_row16(T* dst, const uint32_t* v, float mul, bool store) {
+  uint32_t pk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) pk[e] = pack2<T>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
+  if (store) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    d[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    d[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
 }
 
 __device__ __forceinline__ float2 load2f(const __nv_bfloat16* p) {
@@ -190,11 +280,11 @@ __device__ __forceinline__ uint64_t kstep(int ks, int rows) {
 }
 
 // ---------------------------------------------------------------------------
-// 1. preprocess: Delta and base-2 LSE, padded to whole tiles
+// 1. preprocess: Delta and minus the base-2 LSE, padded to whole tiles
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void ffa_bwd_pre_kernel(const T* __restrict__ o, const T* __restrict__ dout,
-                                   const float* __restrict__ lse, float* __restrict__ lse2,
+                                   const float* __restrict__ lse, float* __restrict__ nlse2,
                                    float* __restrict__ delta, int Hq, int Sq, int Sq_pad, int D, int64_t o_sb,
                                    int64_t o_sh, int64_t o_ss, int64_t d_sb, int64_t d_sh, int64_t d_ss,
                                    int n_rows) {
@@ -221,37 +311,134 @@ __global__ void ffa_bwd_pre_kernel(const T* __restrict__ o, const T* __restrict_
     delta[idx] = acc;
     const float l = (q < Sq) ? lse[(int64_t)bh * Sq + q] : INFINITY;
     // A row that saw no key has LSE = -inf: P is 0 for it, so any finite
-    // offset works; +inf keeps 2^(x - LSE2) at exactly 0.
-    lse2[idx] = (q < Sq && l != -INFINITY) ? l * 1.4426950408889634f : INFINITY;
+    // offset works; -inf keeps 2^(x + NLSE2) at exactly 0.
+    nlse2[idx] = (q < Sq && l != -INFINITY) ? l * -1.4426950408889634f : -INFINITY;
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// shared pieces of the dK/dV and dQ kernels
+// ---------------------------------------------------------------------------
+struct BwdBars {
+  uint64_t fixed_full;    // TMA of the tile the CTA keeps (K/V or Q/dO) landed
+  uint64_t fixed_tmem;    // ... and was copied into TMEM (one arrival per warp of warpgroups 0-1)
+  uint64_t st_full[8];
+  uint64_t st_empty[8];
+  uint64_t sp_full[2];    // S and dP of unit u computed (index u % 2)
+  uint64_t tmem_free[2];  // S and dP of unit u read out of TMEM (one arrival per warp of its pair)
+  uint64_t ds_ready[2];   // P / dS of unit u stored to smem (one arrival per warp of its pair)
+  uint64_t pt_free[2];    // accumulation MMAs of unit u done with its P / dS smem tiles
+  uint64_t acc_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// TMEM columns: the kept tile as the A operand of the S / dP MMAs, then the
+// score buffers (128 columns each: S or S^T, then dP or dP^T), then the fp32
+// accumulators.  dK/dV needs 256 accumulator columns and so has one score
+// buffer; dQ has two.
+constexpr uint32_t TM_FIXED = 0;    // [0, D/2) first kept operand, [64, 64 + D/2) second (16-bit pairs)
+constexpr uint32_t TM_S = 128;      // score buffer b at [128 + 128 b, 256 + 128 b)
+
+__device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns) {
+  mbar_init(&bars->fixed_full, 1);
+  mbar_init(&bars->fixed_tmem, 2 * 4);
+  for (int s = 0; s < ns; ++s) {
+    mbar_init(&bars->st_full[s], 1);
+    mbar_init(&bars->st_empty[s], 1);
+  }
+  for (int t = 0; t < 2; ++t) {
+    mbar_init(&bars->sp_full[t], 1);
+    mbar_init(&bars->tmem_free[t], 2 * 4);
+    mbar_init(&bars->ds_ready[t], 2 * 4);
+    mbar_init(&bars->pt_free[t], 1);
+  }
+  mbar_init(&bars->acc_done, 1);
+  bars->abort = 0;
+  fence_mbar_init();
+}
+
+// Copies row `row` of a 128-row, D-column 16-bit tile from swizzled smem
+// (64-column chunks of 128 rows, as TMA wrote it) into TMEM columns
+// [tcol, tcol + D/2) of this thread's lane: the layout of a K-major A operand.
+template <int D>
+__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, uint32_t tcol) {
+#pragma unroll
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t w[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(tile + c * BWD_BT * 128 + row * 128 + ((j ^ (row & 7)) << 4));
+      w[4 * j] = v.x;
+      w[4 * j + 1] = v.y;
+      w[4 * j + 2] = v.z;
+      w[4 * j + 3] = v.w;
+    }
+    tmem_st32(tcol + 32 * c, w);
+  }
+}
+
+// The MMA issuer's schedule.  S / dP of unit u (into TMEM score buffer
+// u % NBUF) may start once unit u-NBUF's scores are out of TMEM and u's
+// streamed operands have landed; the accumulation MMAs of unit u once its P / dS are in
+// smem.  Whichever is ready goes first, so the tensor core runs one unit's
+// accumulation while the compute warps read the next unit's scores.  The
+// accumulations are issued in unit order, so the sums are deterministic.
+template <int NBUF, typename IssueS, typename IssueAcc>
+__device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_stages, const ErrCtx& ec,
+                                                 volatile int* abort_flag, IssueS issue_s, IssueAcc issue_acc) {
+  int ns = 0, na = 0;
+  long long t_last = clock64();
+  const long long limit = (long long)(ec.limit_ns * 2ull);
+  while (na < n) {
+    bool progressed = false;
+    if (ns < n && mbar_test(&bars->st_full[ns % ns_stages], (ns / ns_stages) & 1) &&
+        (ns < NBUF || mbar_test(&bars->tmem_free[(ns - NBUF) & 1], ((ns - NBUF) >> 1) & 1))) {
+      tc_fence_after();
+      issue_s(ns);
+      mma_commit(&bars->sp_full[ns & 1]);
+      ++ns;
+      progressed = true;
+    }
+    if (na < ns && mbar_test(&bars->ds_ready[na & 1], (na >> 1) & 1)) {
+      tc_fence_after();
+      issue_acc(na);
+      mma_commit(&bars->st_empty[na % ns_stages]);
+      mma_commit(&bars->pt_free[na & 1]);
+      ++na;
+      progressed = true;
+    }
+    if (progressed) {
+      t_last = clock64();
+    } else {
+      if (*abort_flag) return false;
+      if (clock64() - t_last > limit) {
+        *abort_flag = 1;
+        if (ec.err) atomicCAS(ec.err, 0u, (uint32_t)SITE_BWD_DS);
+        return false;
+      }
+    }
+  }
+  return true;
+}
 
 // ---------------------------------------------------------------------------
 // 2. dK / dV
 // ---------------------------------------------------------------------------
 template <int D>
 struct DkdvCfg {
-  static constexpr int TILE = BWD_BT * D * 2;  // K or V tile (128 rows)
-  static constexpr int SUB = BWD_BS * D * 2;   // Q or dO sub-tile (64 rows)
-  static constexpr int NS = D == 64 ? 8 : 4;   // stages of {Q, dO, stats}
+  static constexpr int TILE = BWD_BT * D * 2;     // K or V tile (128 rows)
+  static constexpr int SUB = BWD_BS * D * 2;      // Q or dO sub-tile (64 rows)
+  static constexpr int NS = D == 64 ? 6 : 3;      // stages of {Q, dO, stats}
+  static constexpr int PT = BWD_BT * BWD_BS * 2;  // one P^T or dS^T tile (128 x 64, 16-bit)
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;          // stage s: Q at 2*s*SUB, dO at (2*s+1)*SUB
-  static constexpr int STAT_OFF = STAGE_OFF + NS * 2 * SUB;  // stage s: lse2[64], delta[64]
+  static constexpr int STAGE_OFF = 2 * TILE;               // stage s: Q at 2*s*SUB, dO at (2*s+1)*SUB
+  static constexpr int PT_OFF = STAGE_OFF + NS * 2 * SUB;  // pair b: P^T at b*PT, dS^T at (2+b)*PT
+  static constexpr int STAT_OFF = PT_OFF + 4 * PT;         // stage s: nlse2[64], delta[64]
   static constexpr int BAR_OFF = STAT_OFF + NS * 2 * BWD_BS * 4;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
-};
-
-struct BwdBars {
-  uint64_t fixed_full;    // the tile the CTA keeps (K/V or Q/dO)
-  uint64_t st_full[8];
-  uint64_t st_empty[8];
-  uint64_t sp_full[2];    // S and dP of buffer b computed
-  uint64_t ds_ready[2];   // P / dS of buffer b written back (128 arrivals)
-  uint64_t acc_done;
-  uint32_t tmem_base;
-  int abort;
 };
 
 template <typename T, int D>
@@ -261,11 +448,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         const BwdParams p) {
   using Cfg = DkdvCfg<D>;
   constexpr int NS = Cfg::NS;
+  constexpr int NBUF = 1;
+  constexpr uint32_t TM_ACC = TM_S + 128 * NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + Cfg::K_OFF;
   uint8_t* sV = smem + Cfg::V_OFF;
   uint8_t* sStage = smem + Cfg::STAGE_OFF;
+  uint8_t* sPT = smem + Cfg::PT_OFF;
   float* sStat = reinterpret_cast<float*>(smem + Cfg::STAT_OFF);
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::BAR_OFF);
   volatile int* abort_flag = &bars->abort;
@@ -284,20 +474,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int n = n_i * group;  // units: (query head of the group, 64-row query sub-tile), head-major
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (threadIdx.x == 0) {
-    mbar_init(&bars->fixed_full, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&bars->st_full[s], 1);
-      mbar_init(&bars->st_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars->sp_full[t], 1);
-      mbar_init(&bars->ds_ready[t], 128);
-    }
-    mbar_init(&bars->acc_done, 1);
-    bars->abort = 0;
-    fence_mbar_init();
-  }
+  if (threadIdx.x == 0) bwd_init_bars(bars, NS);
   if (warp == BWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -330,7 +507,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           tma_load_4d(&tmDO, &bars->st_full[s], dst + Cfg::SUB + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
         }
         const int64_t row0 = (int64_t)(b * p.Hq + h) * p.Sq_pad + i * BWD_BS;
-        bulk_load(sStat + 2 * BWD_BS * s, p.lse2 + row0, BWD_BS * 4, &bars->st_full[s]);
+        bulk_load(sStat + 2 * BWD_BS * s, p.nlse2 + row0, BWD_BS * 4, &bars->st_full[s]);
         bulk_load(sStat + 2 * BWD_BS * s + BWD_BS, p.delta + row0, BWD_BS * 4, &bars->st_full[s]);
         ++issued;
       }
@@ -343,103 +520,94 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (K-major x K-major)
-      const uint32_t idesc_acc = make_idesc_f16(128, D, FMT, 0, 1);     // dV, dK (TMEM A x MN-major B)
-      const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
-      const uint64_t v_desc = make_sdesc_sw128(smem_u32(sV), 16, 1024);
+      const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (TMEM A x K-major B)
+      const uint32_t idesc_acc = make_idesc_f16(128, D, FMT, 0, 1);     // dV, dK (K-major A x MN-major B)
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
       const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
-      const uint32_t tDV = tmem + 256, tDK = tmem + 256 + D;
-      // dV += P^T dO and dK += dS^T Q for unit v (after its compute group is done)
-      auto accumulate = [&](int v) -> bool {
-        const int bb = v & 1, s = v % NS;
-        if (!mbar_wait(&bars->ds_ready[bb], (v >> 1) & 1, p.ec, abort_flag, SITE_BWD_DS)) return false;
-        tc_fence_after();
-        const uint64_t q_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
-        const uint64_t do_m = st_mdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
-        const uint32_t tP = tmem + 128 * bb, tDS = tP + 64;
-#pragma unroll
-        for (int ks = 0; ks < BWD_BS / 16; ++ks)
-          mma_ts(tDV, tP + ks * 8, do_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc, (v > 0 || ks > 0) ? 1u : 0u);
-#pragma unroll
-        for (int ks = 0; ks < BWD_BS / 16; ++ks)
-          mma_ts(tDK, tDS + ks * 8, q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc, (v > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(&bars->st_empty[s]);
-        return true;
-      };
-      bool ok = mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      for (int u = 0; u < n && ok; ++u) {
-        const int s = u % NS, bb = u & 1;
-        if (!(ok = mbar_wait(&bars->st_full[s], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
-        tc_fence_after();
+      const uint64_t pt_desc = make_sdesc_sw128(smem_u32(sPT), 16, 1024);
+      const uint32_t tK = tmem + TM_FIXED, tV = tmem + TM_FIXED + 64;
+      const uint32_t tS = tmem + TM_S, tDP = tmem + TM_S + 64;
+      const uint32_t tDV = tmem + TM_ACC, tDK = tmem + TM_ACC + D;
+      auto issue_s = [&](int u) {
+        const int s = u % NS;
         const uint64_t q_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
         const uint64_t do_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
-        const uint32_t tS = tmem + 128 * bb, tDP = tS + 64;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) mma_ss(tS, k_desc + kstep(ks, BWD_BT), q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tK + 8 * ks, q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tDP, v_desc + kstep(ks, BWD_BT), do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
-        mma_commit(&bars->sp_full[bb]);
-        if (u > 0 && !(ok = accumulate(u - 1))) break;
-      }
-      if (ok) ok = accumulate(n - 1);
+        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tDP, tV + 8 * ks, do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+      };
+      auto issue_acc = [&](int v) {
+        const int bb = v & 1, s = v % NS;
+        const uint64_t q_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t do_m = st_mdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint64_t p_k = pt_desc + (uint64_t)((bb * Cfg::PT) >> 4);
+        const uint64_t ds_k = pt_desc + (uint64_t)(((2 + bb) * Cfg::PT) >> 4);
+#pragma unroll
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ss(tDV, p_k + kstep(ks, BWD_BT), do_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc,
+                 (v > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ss(tDK, ds_k + kstep(ks, BWD_BT), q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc,
+                 (v > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, p.ec, abort_flag, issue_s, issue_acc);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
     __syncwarp();
   } else {
     // ------------------------- compute (key rows) -------------------------
-    const int wg = warp / 4;
+    const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;  // key row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * wg, tDP = tS + 64;
+    const uint32_t tS = tmem + lane_off + TM_S + 32 * half, tDP = tS + 64;
     const int key = j * BWD_BT + r;
+    bool ok = true;
+    if (n > 0 && wg < 2) {  // K (warpgroup 0) / V (warpgroup 1) into TMEM as the A operand
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD));
+      if (ok) {
+        tile_row_to_tmem<D>(wg == 0 ? sK : sV, r, tmem + lane_off + TM_FIXED + 64 * wg);
+        tmem_st_wait();
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->fixed_tmem);
+    }
     // Kept query columns of this key, in absolute query positions minus q_offset:
     // causal keeps q >= key - q_offset, the window keeps q <= key + window - 1 - q_offset.
     const int q_keep_lo = p.causal ? key - p.q_offset : -0x3fffffff;
     const int q_keep_hi = key >= p.Skv ? -0x40000000 : (p.window > 0 ? key + p.window - 1 - p.q_offset : 0x3fffffff);
-    bool ok = true;
-    for (int u = wg; u < n; u += 2) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[wg], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
+    for (int u = pair; u < n && ok; u += 2) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[pair], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
       if (!ok) break;
       tc_fence_after();
       const int s = u % NS;
-      const int q0 = (i_lo + u % n_i) * BWD_BS;
-      const float* l2 = sStat + 2 * BWD_BS * s;
-      const float* dl = l2 + BWD_BS;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + hf * 32, sv);
-        tmem_ld32(tDP + hf * 32, dpv);
-        tmem_ld_wait32(sv);
-        tmem_ld_wait32(dpv);
-        int lo;
-        uint32_t cnt;
-        chunk_range(q_keep_lo, q_keep_hi, q0 + hf * 32, lo, cnt);
-        uint32_t pk_p[16], pk_ds[16];
-        bwd_chunk<T, true>(p, sv, dpv, l2 + hf * 32, dl + hf * 32, lo, cnt, pk_p, pk_ds);
-        tmem_st16(tS + hf * 16, pk_p);
-        tmem_st16(tDP + hf * 16, pk_ds);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->ds_ready[wg]);
+      const int q0 = (i_lo + u % n_i) * BWD_BS + 32 * half;
+      const int keep_lo = q_keep_lo - q0, keep_hi = q_keep_hi - q0;
+      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31);
+      const float* nl2 = sStat + 2 * BWD_BS * s + 32 * half;
+      // this pair's P^T / dS^T smem tiles are free once unit u-2's accumulation MMAs are done
+      ok = bwd_unit<T, true, true>(p, tS, tDP, &bars->tmem_free[pair], nl2, nl2 + BWD_BS, 0.f, 0.f, keep_lo,
+                                   keep_hi, masked, &bars->pt_free[pair], u >= 2 ? ((u - 2) >> 1) & 1 : -1,
+                                   abort_flag, sPT + pair * Cfg::PT, sPT + (2 + pair) * Cfg::PT, r, half);
+      if (lane == 0) mbar_arrive(&bars->ds_ready[pair]);
     }
     // ------------------------------ epilogue ------------------------------
-    // warpgroup 0 stores dV, warpgroup 1 stores dK (times the softmax scale)
+    // warpgroups 0 / 2 store dV, 1 / 3 dK (times the softmax scale), each half of the columns
     const bool have = ok && n > 0 &&
                       __all_sync(0xffffffffu, mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DONE));
     if (have) tc_fence_after();
     const bool store = key < p.Skv;
-    T* row = wg == 0
+    T* row = pair == 0
                  ? reinterpret_cast<T*>(p.dv) + (size_t)b * p.dv_sb + (size_t)hkv * p.dv_sh + (size_t)key * p.dv_ss
                  : reinterpret_cast<T*>(p.dk) + (size_t)b * p.dk_sb + (size_t)hkv * p.dk_sh + (size_t)key * p.dk_ss;
-    const uint32_t tacc = tmem + lane_off + 256 + wg * D;
-    const float mul = wg ? p.scale : 1.f;
+    const uint32_t tacc = tmem + lane_off + TM_ACC + pair * D;
+    const float mul = pair ? p.scale : 1.f;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
       uint32_t v[32];
       if (have) {
         tmem_ld32(tacc + c, v);
@@ -464,13 +632,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // ---------------------------------------------------------------------------
 template <int D>
 struct DqCfg {
-  static constexpr int TILE = BWD_BT * D * 2;  // Q or dO tile (128 rows)
-  static constexpr int SUB = BWD_BS * D * 2;   // K or V sub-tile (64 rows)
-  static constexpr int NS = D == 64 ? 8 : 4;   // stages of {K, V}
+  static constexpr int TILE = BWD_BT * D * 2;     // Q or dO tile (128 rows)
+  static constexpr int SUB = BWD_BS * D * 2;      // K or V sub-tile (64 rows)
+  static constexpr int NS = D == 64 ? 8 : 4;      // stages of {K, V}
+  static constexpr int DS = BWD_BT * BWD_BS * 2;  // one dS tile (128 x 64, 16-bit)
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;  // stage s: K at 2*s*SUB, V at (2*s+1)*SUB
-  static constexpr int BAR_OFF = STAGE_OFF + NS * 2 * SUB;
+  static constexpr int STAGE_OFF = 2 * TILE;               // stage s: K at 2*s*SUB, V at (2*s+1)*SUB
+  static constexpr int DS_OFF = STAGE_OFF + NS * 2 * SUB;  // pair b: dS at b*DS
+  static constexpr int BAR_OFF = DS_OFF + 2 * DS;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
@@ -481,11 +651,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       const BwdParams p) {
   using Cfg = DqCfg<D>;
   constexpr int NS = Cfg::NS;
+  constexpr int NBUF = 2;
+  constexpr uint32_t TM_ACC = TM_S + 128 * NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
   uint8_t* sDO = smem + Cfg::DO_OFF;
   uint8_t* sStage = smem + Cfg::STAGE_OFF;
+  uint8_t* sDS = smem + Cfg::DS_OFF;
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::BAR_OFF);
   volatile int* abort_flag = &bars->abort;
 
@@ -503,20 +676,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int n = max(0, j_hi - j_lo);  // units: 64-key sub-tiles
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (threadIdx.x == 0) {
-    mbar_init(&bars->fixed_full, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&bars->st_full[s], 1);
-      mbar_init(&bars->st_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars->sp_full[t], 1);
-      mbar_init(&bars->ds_ready[t], 128);
-    }
-    mbar_init(&bars->acc_done, 1);
-    bars->abort = 0;
-    fence_mbar_init();
-  }
+  if (threadIdx.x == 0) bwd_init_bars(bars, NS);
   if (warp == BWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -559,109 +719,92 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_s = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S, dP (K-major x K-major)
-      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);     // dQ (TMEM A x MN-major B)
-      const uint64_t q_desc = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
-      const uint64_t do_desc = make_sdesc_sw128(smem_u32(sDO), 16, 1024);
+      const uint32_t idesc_s = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S, dP (TMEM A x K-major B)
+      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);     // dQ (K-major A x MN-major B)
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
       const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
-      const uint32_t tDQ = tmem + 256;
-      auto accumulate = [&](int v) -> bool {
-        const int bb = v & 1, s = v % NS;
-        if (!mbar_wait(&bars->ds_ready[bb], (v >> 1) & 1, p.ec, abort_flag, SITE_BWD_DS)) return false;
-        tc_fence_after();
-        const uint64_t k_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
-        const uint32_t tDS = tmem + 128 * bb;
-#pragma unroll
-        for (int ks = 0; ks < BWD_BS / 16; ++ks)
-          mma_ts(tDQ, tDS + ks * 8, k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq, (v > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(&bars->st_empty[s]);
-        return true;
-      };
-      bool ok = mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      for (int u = 0; u < n && ok; ++u) {
-        const int s = u % NS, bb = u & 1;
-        if (!(ok = mbar_wait(&bars->st_full[s], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_LOAD))) break;
-        tc_fence_after();
+      const uint64_t ds_desc = make_sdesc_sw128(smem_u32(sDS), 16, 1024);
+      const uint32_t tQ = tmem + TM_FIXED, tDO = tmem + TM_FIXED + 64;
+      const uint32_t tDQ = tmem + TM_ACC;
+      auto issue_s = [&](int u) {
+        const int s = u % NS;
+        const uint32_t tS = tmem + TM_S + 128 * (u % NBUF), tDP = tS + 64;
         const uint64_t k_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
         const uint64_t v_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
-        const uint32_t tS = tmem + 128 * bb, tDP = tS + 64;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tS, q_desc + kstep(ks, BWD_BT), k_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tDP, do_desc + kstep(ks, BWD_BT), v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
-        mma_commit(&bars->sp_full[bb]);
-        if (u > 0 && !(ok = accumulate(u - 1))) break;
-      }
-      if (ok) ok = accumulate(n - 1);
+        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+      };
+      auto issue_acc = [&](int v) {
+        const int bb = v & 1, s = v % NS;
+        const uint64_t k_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t ds_k = ds_desc + (uint64_t)((bb * Cfg::DS) >> 4);
+#pragma unroll
+        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+          mma_ss(tDQ, ds_k + kstep(ks, BWD_BT), k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq,
+                 (v > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, p.ec, abort_flag, issue_s, issue_acc);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
     __syncwarp();
   } else {
     // ------------------------- compute (query rows) -----------------------
-    const int wg = warp / 4;
+    const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * wg, tDP = tS + 64;
+    const uint32_t tS = tmem + lane_off + TM_S + 128 * (pair % NBUF) + 32 * half, tDP = tS + 64;
     const int row = i * BWD_BT + r;
     const int q_abs = row + p.q_offset;
     const int64_t sidx = (int64_t)(b * p.Hq + h) * p.Sq_pad + row;
-    float l2c[32], dlc[32];
-    {
-      const float l = p.lse2[sidx], d = p.delta[sidx];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        l2c[c] = l;
-        dlc[c] = d;
+    const float row_nl2 = p.nlse2[sidx], row_dl = p.delta[sidx];
+    bool ok = true;
+    if (n > 0 && wg < 2) {  // Q (warpgroup 0) / dO (warpgroup 1) into TMEM as the A operand
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD));
+      if (ok) {
+        tile_row_to_tmem<D>(wg == 0 ? sQ : sDO, r, tmem + lane_off + TM_FIXED + 64 * wg);
+        tmem_st_wait();
+        tc_fence_before();
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->fixed_tmem);
     }
     // kept keys of this row: [q_abs - window + 1, min(q_abs, Skv - 1)]
     const int k_keep_lo = p.window > 0 ? q_abs - p.window + 1 : -0x3fffffff;
     const int k_keep_hi = min(p.causal ? q_abs : 0x3fffffff, p.Skv - 1);
-    bool ok = true;
-    for (int u = wg; u < n; u += 2) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[wg], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
+    for (int u = pair; u < n && ok; u += 2) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[pair], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
       if (!ok) break;
       tc_fence_after();
-      const int c0 = (j_lo + u) * BWD_BS;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld32(tS + hf * 32, sv);
-        tmem_ld32(tDP + hf * 32, dpv);
-        tmem_ld_wait32(sv);
-        tmem_ld_wait32(dpv);
-        int lo;
-        uint32_t cnt;
-        chunk_range(k_keep_lo, k_keep_hi, c0 + hf * 32, lo, cnt);
-        uint32_t pk_ds[16];
-        bwd_chunk<T, false>(p, sv, dpv, l2c, dlc, lo, cnt, nullptr, pk_ds);
-        tmem_st16(tS + hf * 16, pk_ds);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->ds_ready[wg]);
+      const int c0 = (j_lo + u) * BWD_BS + 32 * half;
+      const int keep_lo = k_keep_lo - c0, keep_hi = k_keep_hi - c0;
+      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31);
+      ok = bwd_unit<T, false, false>(p, tS, tDP, &bars->tmem_free[pair], nullptr, nullptr, row_nl2, row_dl,
+                                     keep_lo, keep_hi, masked, &bars->pt_free[pair],
+                                     u >= 2 ? ((u - 2) >> 1) & 1 : -1, abort_flag, nullptr, sDS + pair * Cfg::DS, r,
+                                     half);
+      if (lane == 0) mbar_arrive(&bars->ds_ready[pair]);
     }
-    // epilogue: warpgroup 0 stores dQ columns [0, D/2), warpgroup 1 the rest
+    // epilogue: warpgroup w stores dQ columns [w D/4, (w+1) D/4)
     const bool have = ok && n > 0 &&
                       __all_sync(0xffffffffu, mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DONE));
     if (have) tc_fence_after();
     const bool store = row < p.Sq;
     T* dqrow = reinterpret_cast<T*>(p.dq) + (size_t)b * p.dq_sb + (size_t)h * p.dq_sh + (size_t)row * p.dq_ss;
 #pragma unroll
-    for (int c = wg * (D / 2); c < (wg + 1) * (D / 2); c += 32) {
-      uint32_t v[32];
+    for (int c = wg * (D / 4); c < (wg + 1) * (D / 4); c += 16) {
+      uint32_t v[16];
       if (have) {
-        tmem_ld32(tmem + lane_off + 256 + c, v);
-        tmem_ld_wait32(v);
+        tmem_ld16(tmem + lane_off + TM_ACC + c, v);
+        tmem_ld_wait16(v);
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = 0u;
+        for (int e = 0; e < 16; ++e) v[e] = 0u;
       }
-      store_row32<T>(dqrow + c, v, p.scale, store);
+      store_row16<T>(dqrow + c, v, p.scale, store);
     }
   }
   tc_fence_before();
@@ -765,7 +908,7 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
   uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 127) & ~uintptr_t(127);
   float* lse2 = reinterpret_cast<float*>(ws);
   float* delta = lse2 + (size_t)B * Hq * p.Sq_pad;
-  p.lse2 = lse2;
+  p.nlse2 = lse2;
   p.delta = delta;
   p.B = B;
   p.Hq = Hq;

@@ -250,6 +250,10 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       FFA_I8(r, 0), FFA_I8(r, 8)
       : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), FFA_I8(r, 0)
+               : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Generic-proxy smem writes -> visible to the async proxy (tensor core / TMA).

@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     mbar_init(&bars->q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      for (int k = 0; k < FWD_PCH; ++k) mbar_init(&bars->p_full[t][k], FWD_BM);
+      for (int k = 0; k < FWD_PCH; ++k) mbar_init(&bars->p_full[t][k], FWD_BM / 32);  // one arrival per warp
       mbar_init(&bars->o_done[t], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_st16(tS + k * 16, pk);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars->p_full[t][k]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[t][k]);
       }
       const float2 acct = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
       l += acct.x + acct.y;
