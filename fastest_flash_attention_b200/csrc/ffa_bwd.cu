@@ -393,15 +393,15 @@ __device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_st
   const long long limit = (long long)(ec.limit_ns * 2ull);
   while (na < n) {
     bool progressed = false;
-    if (ns < n && mbar_test(&bars->st_full[ns % ns_stages], (ns / ns_stages) & 1) &&
-        (ns < NBUF || mbar_test(&bars->tmem_free[(ns - NBUF) & 1], ((ns - NBUF) >> 1) & 1))) {
+    if (ns < n && mbar_poll(&bars->st_full[ns % ns_stages], (ns / ns_stages) & 1) &&
+        (ns < NBUF || mbar_poll(&bars->tmem_free[(ns - NBUF) & 1], ((ns - NBUF) >> 1) & 1))) {
       tc_fence_after();
       issue_s(ns);
       mma_commit(&bars->sp_full[ns & 1]);
       ++ns;
       progressed = true;
     }
-    if (na < ns && mbar_test(&bars->ds_ready[na & 1], (na >> 1) & 1)) {
+    if (na < ns && mbar_poll(&bars->ds_ready[na & 1], (na >> 1) & 1)) {
       tc_fence_after();
       issue_acc(na);
       mma_commit(&bars->st_empty[na % ns_stages]);

@@ -76,6 +76,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe (test_wait never suspends the thread, unlike try_wait):
+// for issuers that poll several barriers and take whichever is ready.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  The wait is bounded
 // by wall-clock time: on expiry the site code is recorded in the error word,
 // `*abort` is raised so every other role of the CTA stops waiting too, and

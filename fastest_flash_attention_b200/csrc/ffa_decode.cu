@@ -382,21 +382,11 @@ static int launch_decode(const CUtensorMap& mk, const CUtensorMap& mv, const Dec
 // query (q_lat = q_nope W_UK per head) and applied after attention
 // (out = o_lat W_UV^T), decoding is multi-query attention of every head over
 // the shared latent keys [c_kv | k_rope] with values c_kv.  One CTA per
-// (split, request); the chunk of 16 tokens x 576 values is loaded once and
-// serves as both K and V.  The 4 consumer warps split Q.K^T over the key
-// dims (partial scores summed through smem in MMA-fragment order, so no
-// layout change) and split O over the value dims.
+// (split, request), splits merged by LSE.
 // ---------------------------------------------------------------------------
 constexpr int MLA_LAT = 512, MLA_ROPE = 64, MLA_DK = MLA_LAT + MLA_ROPE;
-constexpr int MLA_HEADS = 32;  // two m16 tiles of query heads per CTA
-constexpr int MLA_STAGES = 4;
-constexpr int MLA_BOXES = MLA_DK / 64;           // 9 swizzled 64-column boxes per chunk
-constexpr int MLA_STAGE = MLA_BOXES * DEC_CHUNK * 128;  // 18 KB
-constexpr int MLA_KSTEPS = MLA_DK / 16 / DEC_CONSUMERS;  // 9 k-steps of the scores per warp
-constexpr int MLA_XS_OFF = MLA_STAGES * MLA_STAGE;
-constexpr int MLA_XS_BYTES = 2 * DEC_CONSUMERS * 32 * 16 * 4;
-constexpr int MLA_BAR_OFF = MLA_XS_OFF + MLA_XS_BYTES;
-constexpr int MLA_SMEM = MLA_BAR_OFF + 256 + 1024;
+constexpr int MLA_HEADS = 32;  // query heads: the N dimension of both tensor-core products
+constexpr int MLA_BOXES = MLA_DK / 64;  // 9 swizzled 64-column boxes per token row
 
 struct MlaParams {
   const void* q;  // [R, H, 576] = [q_lat | q_rope]
@@ -407,214 +397,431 @@ struct MlaParams {
   float* o_part;    // [R, max_splits, H, 512]
   float* lse_part;  // [R, max_splits, H] (base 2)
   int R, H, page_size, max_splits, chunks_per_split;
+  int box_rows;  // token rows per TMA box of the latent decode kernel: gcd(page_size, 128)
   float scale_log2;
   ErrCtx ec;
 };
 
+// ---------------------------------------------------------------------------
+// MLA absorbed decode on the 5th-generation tensor cores.
+//
+// Tokens are the M dimension of both products, so 32 heads fit the MMA shape
+// without padding:
+//   S^T [128 tokens x 32 heads] = C [128 x 576] . Q^T          (K = 576)
+//   O^T [512 dims x 32 heads]  += C_lat^T [512 x 128] . P^T     (K = 128 tokens)
+// C is read once per tile of 128 tokens and serves both products: the latent
+// part (512 dims) as the M-major A operand of the second.  Roles:
+//   warps 0-7  softmax (thread r % 128 = token r of the tile; warpgroup g
+//              takes heads [16 g, 16 g + 16)): per-head maximum over the
+//              tile's tokens by a transposing butterfly of warp shuffles plus
+//              a cross-warp exchange in smem, P^T = 2^(s*scale*log2e - m)
+//              stored to smem as the B operand of O^T, running row sums; O^T
+//              is rescaled (exactly, numerator and denominator alike) only
+//              when a head's maximum grows by more than 2^8.
+//   warp 8     TMA producer: boxes of gcd(page_size, 128) tokens through the
+//              block table into a ring of 5 slots (4 slots of 2 latent
+//              boxes, 1 rope box).
+//   warp 9     MMA issuer, TMEM owner.
+// TMEM: O^T in columns [0, 128) (block m of 128 dims at 32 m), S^T double
+// buffered at [128, 192).
+// ---------------------------------------------------------------------------
+constexpr int MLT_TILE = 128;                 // tokens per tile (MMA M)
+constexpr int MLT_BOX = MLT_TILE * 128;       // one 64-dim box of the tile: 16 KB
+constexpr int MLT_SLOT = 2 * MLT_BOX;         // 32 KB
+constexpr int MLT_NSLOT = 5;
+constexpr int MLT_Q_OFF = MLT_NSLOT * MLT_SLOT;               // 9 boxes of [32 heads x 64 dims]
+constexpr int MLT_QBOX = MLA_HEADS * 128;                     // 4 KB
+constexpr int MLT_P_OFF = MLT_Q_OFF + MLA_BOXES * MLT_QBOX;  // 2 buffers of P^T [32 x 128]
+constexpr int MLT_PBUF = MLA_HEADS * MLT_TILE * 2;            // 8 KB
+constexpr int MLT_RED_OFF = MLT_P_OFF + 2 * MLT_PBUF;         // [2][4 warps][32] floats
+constexpr int MLT_BAR_OFF = MLT_RED_OFF + 2 * 4 * 32 * 4;
+constexpr int MLT_SMEM = MLT_BAR_OFF + 256 + 1024;
+constexpr int MLT_THREADS = 320;
+constexpr float MLT_RESCALE = 8.0f;
+
+struct MltBars {
+  uint64_t slot_full[MLT_NSLOT];
+  uint64_t slot_empty[MLT_NSLOT];
+  uint64_t q_ready;     // Q stored to smem (one arrival per softmax warp)
+  uint64_t s_full[2];   // S^T of tile t computed
+  uint64_t p_ready[2];  // P^T of tile t stored (one arrival per softmax warp)
+  uint64_t o_done[2];   // O^T MMAs of tile t retired
+  uint64_t red_full[2]; // per-warp partial maxima / sums of a tile exchanged
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// Transposing butterfly over 16 columns: lanes i and i + 16 end with the
+// maximum (MAX) or sum over the 32 lanes of v[i % 16].  16 shuffles.
+template <bool MAX>
+__device__ __forceinline__ float warp_colreduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float keep = up ? v[i + o] : v[i];
+      const float give = up ? v[i] : v[i + o];
+      const float got = __shfl_xor_sync(0xffffffffu, give, o);
+      v[i] = MAX ? fmaxf(keep, got) : keep + got;
+    }
+  }
+  const float other = __shfl_xor_sync(0xffffffffu, v[0], 16);
+  return MAX ? fmaxf(v[0], other) : v[0] + other;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(DEC_THREADS)
-    ffa_mla_decode_kernel(const __grid_constant__ CUtensorMap tmC, const MlaParams p) {
+__global__ void __launch_bounds__(128) ffa_mla_merge_kernel(const float* __restrict__ o_part,
+                                                            const float* __restrict__ lse_part,
+                                                            const int* __restrict__ ctx_lens, void* out,
+                                                            float* lse_out, int H, int max_splits,
+                                                            int chunks_per_split, int64_t o_sr, int64_t o_sh) {
+  const int r = blockIdx.x / H, head = blockIdx.x % H;
+  const int n_chunks = (ctx_lens[r] + DEC_CHUNK - 1) / DEC_CHUNK;
+  const int ns = (n_chunks + chunks_per_split - 1) / chunks_per_split;
+  const int64_t base = (int64_t)r * max_splits * H + head;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, lse_part[base + (int64_t)s * H]);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int s = 0; s < ns; ++s) {
+    const int64_t pidx = base + (int64_t)s * H;
+    const float ls = lse_part[pidx];
+    const float f = (ls == -INFINITY) ? 0.f : ex2(ls - M);
+    const float4 v = reinterpret_cast<const float4*>(o_part + pidx * MLA_LAT)[threadIdx.x];
+    L += f;
+    acc.x += f * v.x;
+    acc.y += f * v.y;
+    acc.z += f * v.z;
+    acc.w += f * v.w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  T* orow = reinterpret_cast<T*>(out) + (int64_t)r * o_sr + (int64_t)head * o_sh + 4 * threadIdx.x;
+  const uint32_t lo = pack2<T>(acc.x * inv, acc.y * inv), hi = pack2<T>(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(orow) = make_uint2(lo, hi);
+  if (threadIdx.x == 0 && lse_out)
+    lse_out[(int64_t)r * H + head] = (L > 0.f) ? (M + lg2(L)) * 0.6931471805599453f : -INFINITY;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(MLT_THREADS, 1)
+    ffa_mla_decode_tc_kernel(const __grid_constant__ CUtensorMap tmC, const MlaParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + MLA_BAR_OFF);
-  uint64_t* empty = full + MLA_STAGES;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + MLA_STAGES);
-  float* xs = reinterpret_cast<float*>(smem + MLA_XS_OFF);
+  MltBars* bars = reinterpret_cast<MltBars*>(smem + MLT_BAR_OFF);
+  float* red = reinterpret_cast<float*>(smem + MLT_RED_OFF);
+  volatile int* abort_flag = &bars->abort;
 
   const int split = blockIdx.x, r = blockIdx.y;
   const int ctx = p.ctx_lens[r];
   const int n_chunks = (ctx + DEC_CHUNK - 1) / DEC_CHUNK;
   const int c_begin = split * p.chunks_per_split;
   if (c_begin >= n_chunks) return;
-  const int n = min(n_chunks, c_begin + p.chunks_per_split) - c_begin;
+  const int c_end = min(n_chunks, c_begin + p.chunks_per_split);
+  const int tok_end = min(ctx, c_end * DEC_CHUNK);  // tokens of this split: [c_begin*16, tok_end)
+  const int n_tiles = (c_end - c_begin + 7) / 8;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int sub_per_page = p.page_size / DEC_CHUNK;
+  constexpr uint32_t FMT = DtypeFmt<T>::value;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < MLA_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], DEC_CONSUMERS);
+    for (int s = 0; s < MLT_NSLOT; ++s) {
+      mbar_init(&bars->slot_full[s], 1);
+      mbar_init(&bars->slot_empty[s], 1);
     }
-    *abort_flag = 0;
+    mbar_init(&bars->q_ready, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->s_full[b], 1);
+      mbar_init(&bars->p_ready[b], 8);
+      mbar_init(&bars->o_done[b], 1);
+      mbar_init(&bars->red_full[b], 8);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
     fence_mbar_init();
   }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
 
-  if (warp == DEC_CONSUMERS) {
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      const int* table = p.block_table + (int64_t)r * p.bt_stride;
-      int issued = 0;
-      for (int idx = 0; idx < n; ++idx) {
-        const int s = idx % MLA_STAGES, use = idx / MLA_STAGES;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_DEC_EMPTY)) break;
-        const int c = c_begin + idx;
-        const int row = table[c / sub_per_page] * p.page_size + (c % sub_per_page) * DEC_CHUNK;
-        mbar_arrive_expect_tx(&full[s], MLA_STAGE);
-        uint8_t* dst = smem + s * MLA_STAGE;
-#pragma unroll
-        for (int bx = 0; bx < MLA_BOXES; ++bx)
-          tma_load_4d(&tmC, &full[s], dst + bx * DEC_CHUNK * 128, bx * 64, row, 0, 0, pol);
+  if (warp == 8) {
+    // ------------------------------ producer ------------------------------
+    // The split's page ids are read 32 at a time, one per lane, and handed to
+    // the issuing lane by shuffles, so no TMA issue waits on a global load.
+    const uint64_t pol = policy_evict_first();
+    const int* table = p.block_table + (int64_t)r * p.bt_stride;
+    const int br = p.box_rows;
+    const int page0 = c_begin * DEC_CHUNK / p.page_size;
+    const int n_pages_req = (ctx + p.page_size - 1) / p.page_size;
+    const int n_blk = (ctx + br - 1) / br;  // br-row blocks holding the request's tokens
+    int win = -1, pid = 0;  // page window [32 win, 32 win + 32) held by the lanes
+    int issued = 0;
+    bool ok = true;
+    for (int t = 0; t < n_tiles && ok; ++t) {
+      for (int kk = 0; kk < MLT_NSLOT && ok; ++kk) {
+        const int k = (kk + MLT_NSLOT - 1) % MLT_NSLOT;  // the rope slot first: it frees earliest
+        if (t > 0)
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->slot_empty[k], (t - 1) & 1, p.ec, abort_flag, SITE_DEC_EMPTY));
+        if (!ok) break;
+        const int nbox = k < 4 ? 2 : 1;
+        if (lane == 0) mbar_arrive_expect_tx(&bars->slot_full[k], nbox * MLT_BOX);
+        uint8_t* dst = smem + k * MLT_SLOT;
+        for (int sub = 0; sub < MLT_TILE / br; ++sub) {
+          // blocks past the request reload its last block: finite values, masked by P = 0
+          const int blk = min((c_begin * DEC_CHUNK + t * MLT_TILE) / br + sub, n_blk - 1);
+          const int pg = blk * br / p.page_size - page0;
+          if (pg / 32 != win) {
+            win = pg / 32;
+            const int idx = page0 + 32 * win + lane;
+            pid = idx < n_pages_req ? table[idx] : 0;
+          }
+          const int page = __shfl_sync(0xffffffffu, pid, pg % 32);
+          const int row = page * p.page_size + (blk * br) % p.page_size;
+          if (lane == 0)
+            for (int bx = 0; bx < nbox; ++bx) {
+              const int box = k < 4 ? 2 * k + bx : 8;
+              tma_load_4d(&tmC, &bars->slot_full[k], dst + bx * MLT_BOX + sub * br * 128, box * 64, row, 0, 0, pol);
+            }
+        }
         ++issued;
       }
-      if (*abort_flag)
-        for (int q = max(0, issued - MLA_STAGES); q < issued; ++q)
-          mbar_wait(&full[q % MLA_STAGES], (q / MLA_STAGES) & 1, p.ec, abort_flag, SITE_DEC_FULL, true);
     }
-    return;
-  }
-
-  const int g = lane >> 2, t = lane & 3;
-  const int mi = lane >> 3, mr = lane & 7;
-  // This warp's slice of Q (k-steps 9w .. 9w+8) for both 16-head row tiles.
-  uint32_t qa[MLA_KSTEPS][2][4];
-  {
-    const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)r * p.q_sr;
-#pragma unroll
-    for (int i = 0; i < MLA_KSTEPS; ++i) {
-      const int d = (warp * MLA_KSTEPS + i) * 16 + 2 * t;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-          const T* qr = qb + (int64_t)(mt * 16 + g + 8 * hi) * p.q_sh + d;
-          qa[i][mt][hi] = *reinterpret_cast<const uint32_t*>(qr);
-          qa[i][mt][2 + hi] = *reinterpret_cast<const uint32_t*>(qr + 8);
-        }
-    }
-  }
-  float o[2][16][4];  // [row tile][8-dim n-tile of this warp's 128 value dims][frag]
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[mt][i][0] = o[mt][i][1] = o[mt][i][2] = o[mt][i][3] = 0.f;
-  float m_r[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};  // [row tile][lo/hi]
-  float l_r[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-
-  bool ok = true;
-  for (int idx = 0; idx < n; ++idx) {
-    const int s = idx % MLA_STAGES;
-    // No early exit: every consumer warp must reach the named barrier below
-    // once per chunk.  After an expired wait (abort) the waits return at
-    // once and the stale smem is only read, so the loop drains quickly; the
-    // error word reports the failure.
-    ok = mbar_wait(&full[s], (idx / MLA_STAGES) & 1, p.ec, abort_flag, SITE_DEC_FULL) && ok;
+    if (lane == 0 && *abort_flag)  // copies in flight must land before the CTA exits
+      for (int q = max(0, issued - MLT_NSLOT); q < issued; ++q)
+        mbar_wait(&bars->slot_full[(q % MLT_NSLOT + MLT_NSLOT - 1) % MLT_NSLOT], (q / MLT_NSLOT) & 1, p.ec,
+                  abort_flag, SITE_DEC_FULL, true);
     __syncwarp();
-    const uint32_t cbase = smem_u32(smem + s * MLA_STAGE);
-    float sc[2][2][4];  // [row tile][token n-tile][frag]
+  } else if (warp == 9) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc_f16(128, MLA_HEADS, FMT, 0, 0);  // C (K-major) x Q (K-major)
+      const uint32_t idesc_o = make_idesc_f16(128, MLA_HEADS, FMT, 1, 0);  // C_lat^T (M-major) x P^T (K-major)
+      const uint64_t c_kdesc = make_sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t c_mdesc = make_sdesc_sw128(smem_u32(smem), MLT_BOX, 1024);
+      const uint64_t q_desc = make_sdesc_sw128(smem_u32(smem + MLT_Q_OFF), 16, 1024);
+      const uint64_t p_desc = make_sdesc_sw128(smem_u32(smem + MLT_P_OFF), 16, 1024);
+      bool ok = mbar_wait(&bars->q_ready, 0, p.ec, abort_flag, SITE_DEC_FULL);
+      auto issue_o = [&](int t) -> bool {
+        if (!mbar_wait(&bars->p_ready[t & 1], (t >> 1) & 1, p.ec, abort_flag, SITE_DEC_FULL)) return false;
+        tc_fence_after();
+        const uint64_t pb = p_desc + (uint64_t)(((t & 1) * MLT_PBUF) >> 4);
+        for (int m = 0; m < 4; ++m) {
+          const uint64_t a = c_mdesc + (uint64_t)((m * MLT_SLOT) >> 4);
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
-#pragma unroll
-    for (int i = 0; i < MLA_KSTEPS; ++i) {
-      const int kk = warp * MLA_KSTEPS + i;
-      const int bx = kk / 4, ch = 2 * (kk % 4) + (mi & 1), tok = mr + 8 * (mi >> 1);
-      uint32_t b00, b01, b10, b11;
-      ldsm_x4(sw128(cbase + bx * DEC_CHUNK * 128, tok, ch), b00, b01, b10, b11);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        mma16816<T>(sc[mt][0], qa[i][mt], b00, b01);
-        mma16816<T>(sc[mt][1], qa[i][mt], b10, b11);
-      }
-    }
-    // Sum the four warps' partial scores (same fragment positions in every warp).
-    float* xw = xs + ((idx & 1) * DEC_CONSUMERS + warp) * 32 * 16 + lane * 16;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) xw[e] = sc[e / 8][(e / 4) % 2][e % 4];
-    asm volatile("bar.sync 1, %0;" ::"n"(DEC_CONSUMERS * 32) : "memory");
-    float x[2][2][4];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < DEC_CONSUMERS; ++w) v += xs[((idx & 1) * DEC_CONSUMERS + w) * 32 * 16 + lane * 16 + e];
-      const int nt = (e / 4) % 2;
-      const int tok = (c_begin + idx) * DEC_CHUNK + nt * 8 + 2 * t + (e & 1);
-      x[e / 8][nt][e % 4] = tok < ctx ? v * p.scale_log2 : -INFINITY;
-    }
-    // online softmax per row (identical in every warp)
-    uint32_t pa[2][4];
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      float mx_lo = fmaxf(fmaxf(x[mt][0][0], x[mt][0][1]), fmaxf(x[mt][1][0], x[mt][1][1]));
-      float mx_hi = fmaxf(fmaxf(x[mt][0][2], x[mt][0][3]), fmaxf(x[mt][1][2], x[mt][1][3]));
-#pragma unroll
-      for (int off = 1; off < 4; off <<= 1) {
-        mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
-        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
-      }
-      const float mn_lo = fmaxf(m_r[mt][0], mx_lo), mn_hi = fmaxf(m_r[mt][1], mx_hi);
-      if (__any_sync(0xffffffffu, mn_lo > m_r[mt][0] + 8.f || mn_hi > m_r[mt][1] + 8.f)) {
-        const float a_lo = (mn_lo == -INFINITY) ? 1.f : ex2(m_r[mt][0] - mn_lo);
-        const float a_hi = (mn_hi == -INFINITY) ? 1.f : ex2(m_r[mt][1] - mn_hi);
-        l_r[mt][0] *= a_lo;
-        l_r[mt][1] *= a_hi;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          o[mt][i][0] *= a_lo;
-          o[mt][i][1] *= a_lo;
-          o[mt][i][2] *= a_hi;
-          o[mt][i][3] *= a_hi;
+          for (int ks = 0; ks < MLT_TILE / 16; ++ks)
+            mma_ss(tmem + 32 * m, a + (uint64_t)((ks * 16 * 128) >> 4),
+                   pb + (uint64_t)(((ks / 4) * (MLA_HEADS * 128) + (ks % 4) * 32) >> 4), idesc_o,
+                   (t > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&bars->slot_empty[m]);
         }
-        m_r[mt][0] = mn_lo;
-        m_r[mt][1] = mn_hi;
+        mma_commit(&bars->o_done[t & 1]);
+        return true;
+      };
+      // O^T(t-1) goes before S^T(t): the loads of tile t wait for the slots
+      // that O^T(t-1) releases.
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        if (t > 0 && !(ok = issue_o(t - 1))) break;
+        const uint32_t dS = tmem + 128 + 32 * (t & 1);
+        bool first = true;
+        for (int kk = 0; kk < MLT_NSLOT && ok; ++kk) {
+          const int k = (kk + MLT_NSLOT - 1) % MLT_NSLOT;
+          if (!(ok = mbar_wait(&bars->slot_full[k], t & 1, p.ec, abort_flag, SITE_DEC_FULL))) break;
+          tc_fence_after();
+          const int nbox = k < 4 ? 2 : 1;
+          for (int bx = 0; bx < nbox; ++bx) {
+            const int box = k < 4 ? 2 * k + bx : 8;
+            const uint64_t a = c_kdesc + (uint64_t)((k * MLT_SLOT + bx * MLT_BOX) >> 4);
+            const uint64_t b = q_desc + (uint64_t)((box * MLT_QBOX) >> 4);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              mma_ss(dS, a + (uint64_t)(ks * 2), b + (uint64_t)(ks * 2), idesc_s, first ? 0u : 1u);
+              first = false;
+            }
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bars->slot_empty[4]);  // the rope box is not needed by O^T
+        mma_commit(&bars->s_full[t & 1]);
       }
-      const float u_lo = (m_r[mt][0] == -INFINITY) ? 0.f : m_r[mt][0];
-      const float u_hi = (m_r[mt][1] == -INFINITY) ? 0.f : m_r[mt][1];
-      float pr[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        pr[nt][0] = ex2(x[mt][nt][0] - u_lo);
-        pr[nt][1] = ex2(x[mt][nt][1] - u_lo);
-        pr[nt][2] = ex2(x[mt][nt][2] - u_hi);
-        pr[nt][3] = ex2(x[mt][nt][3] - u_hi);
-        l_r[mt][0] += pr[nt][0] + pr[nt][1];
-        l_r[mt][1] += pr[nt][2] + pr[nt][3];
-      }
-      pa[mt][0] = pack2<T>(pr[0][0], pr[0][1]);
-      pa[mt][1] = pack2<T>(pr[0][2], pr[0][3]);
-      pa[mt][2] = pack2<T>(pr[1][0], pr[1][1]);
-      pa[mt][3] = pack2<T>(pr[1][2], pr[1][3]);
-    }
-    // O[:, 128w .. 128w+127] += P V  (V = the chunk's latent columns)
-#pragma unroll
-    for (int nt = 0; nt < 16; nt += 2) {
-      const int d = warp * 128 + nt * 8;
-      const int bx = d / 64, ch = (d % 64) / 8 + (mi >> 1), tok = mr + 8 * (mi & 1);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(sw128(cbase + bx * DEC_CHUNK * 128, tok, ch), b0, b1, b2, b3);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        mma16816<T>(o[mt][nt], pa[mt], b0, b1);
-        mma16816<T>(o[mt][nt + 1], pa[mt], b2, b3);
+      if (ok && n_tiles > 0) ok = issue_o(n_tiles - 1);
+      if (!ok) {  // let issued MMAs retire before TMEM is released
+        mma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, p.ec, abort_flag, SITE_DEC_FULL, true);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  // Full row sums, then this warp's value dims of the split result.
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi)
-#pragma unroll
-      for (int off = 1; off < 4; off <<= 1) l_r[mt][hi] += __shfl_xor_sync(0xffffffffu, l_r[mt][hi], off);
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-      const int head = mt * 16 + g + 8 * hi;
-      const int64_t pidx = ((int64_t)r * p.max_splits + split) * p.H + head;
-      const float L = l_r[mt][hi];
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      float* dst = p.o_part + pidx * MLA_LAT + warp * 128;
-#pragma unroll
-      for (int nt = 0; nt < 16; ++nt)
-        *reinterpret_cast<float2*>(dst + nt * 8 + 2 * t) =
-            make_float2(o[mt][nt][2 * hi] * inv, o[mt][nt][2 * hi + 1] * inv);
-      if (warp == 0 && t == 0) p.lse_part[pidx] = (L > 0.f) ? m_r[mt][hi] + lg2(L) : -INFINITY;
+  } else {
+    // ------------------------------ softmax -------------------------------
+    // warpgroup hh handles heads [16 hh, 16 hh + 16) of every token
+    const int tr = threadIdx.x % 128;  // token row of the tile = TMEM lane
+    const int hh = warp / 4;
+    const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+    // Q -> smem as 9 K-major swizzled boxes of [32 heads x 64 dims]
+    {
+      const T* qr = reinterpret_cast<const T*>(p.q) + (int64_t)r * p.q_sr;
+      for (int c = threadIdx.x; c < MLA_HEADS * (MLA_DK / 8); c += 256) {
+        const int h = c / (MLA_DK / 8), j = c % (MLA_DK / 8);
+        const uint4 v = *reinterpret_cast<const uint4*>(qr + (int64_t)h * p.q_sh + j * 8);
+        const int box = j / 8, jj = j % 8;
+        *reinterpret_cast<uint4*>(smem + MLT_Q_OFF + box * MLT_QBOX + h * 128 + ((jj ^ (h & 7)) << 4)) = v;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->q_ready);
     }
+    float m_run[16], l_part[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      m_run[h] = -INFINITY;
+      l_part[h] = 0.f;
+    }
+    // this warpgroup's 4 per-warp partials of head j: red[buf][4 hh + w][j]
+    auto wg_reduce = [&](const float* rb, float (&out)[16], bool is_max) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 acc = reinterpret_cast<const float4*>(rb + (4 * hh) * 16)[q];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+          const float4 v = reinterpret_cast<const float4*>(rb + (4 * hh + w) * 16)[q];
+          acc.x = is_max ? fmaxf(acc.x, v.x) : acc.x + v.x;
+          acc.y = is_max ? fmaxf(acc.y, v.y) : acc.y + v.y;
+          acc.z = is_max ? fmaxf(acc.z, v.z) : acc.z + v.z;
+          acc.w = is_max ? fmaxf(acc.w, v.w) : acc.w + v.w;
+        }
+        out[4 * q] = acc.x;
+        out[4 * q + 1] = acc.y;
+        out[4 * q + 2] = acc.z;
+        out[4 * q + 3] = acc.w;
+      }
+    };
+    bool ok = true;
+    for (int t = 0; t < n_tiles && ok; ++t) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[t & 1], (t >> 1) & 1, p.ec, abort_flag, SITE_DEC_FULL));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[16];
+      tmem_ld16(tmem + lane_off + 128 + 32 * (t & 1) + 16 * hh, sv);
+      tmem_ld_wait16(sv);
+      const bool valid = c_begin * DEC_CHUNK + t * MLT_TILE + tr < tok_end;
+      float x[16], v[16];
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        x[h] = valid ? __uint_as_float(sv[h]) * p.scale_log2 : -INFINITY;
+        v[h] = x[h];
+      }
+      // per-head tile maximum: warp butterfly, then the warpgroup's 4 warps through smem
+      float* rb = red + (t & 1) * 128;
+      const float wm = warp_colreduce16<true>(v, lane);
+      if (lane < 16) rb[warp * 16 + lane] = wm;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->red_full[t & 1]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->red_full[t & 1], (t >> 1) & 1, p.ec, abort_flag, SITE_DEC_FULL));
+      if (!ok) break;
+      // heads whose maximum grew past the threshold move it, and rescale
+      float mt[16], alpha[16];
+      wg_reduce(rb, mt, true);
+      bool resc = false;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        alpha[h] = 1.f;
+        if (mt[h] > m_run[h] + MLT_RESCALE) {
+          alpha[h] = m_run[h] == -INFINITY ? 0.f : ex2(m_run[h] - mt[h]);
+          m_run[h] = mt[h];
+          l_part[h] *= alpha[h];
+          resc = true;
+        }
+      }
+      // O^T and this buffer of P^T must be done with tile t-1 / t-2: both
+      // follow from O^T(t-1) having retired (the tensor core runs in order).
+      if (t > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bars->o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.ec, abort_flag, SITE_DEC_FULL));
+        if (!ok) break;
+        tc_fence_after();
+        if (resc) {
+          // thread tr owns dim tr of each 128-dim block of O^T
+#pragma unroll 1
+          for (int m = 0; m < 4; ++m) {
+            uint32_t ov[16];
+            tmem_ld16(tmem + lane_off + 32 * m + 16 * hh, ov);
+            tmem_ld_wait16(ov);
+#pragma unroll
+            for (int h = 0; h < 16; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+            tmem_st16(tmem + lane_off + 32 * m + 16 * hh, ov);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P^T[h][tr] (K-major B of O^T: head rows, token columns in two 64-token chunks)
+      uint8_t* pb = smem + MLT_P_OFF + (t & 1) * MLT_PBUF + (tr / 64) * (MLA_HEADS * 128);
+      const int tc = tr % 64;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int h = 16 * hh + j;
+        const float pv = ex2(x[j] - (m_run[j] == -INFINITY ? 0.f : m_run[j]));
+        l_part[j] += pv;
+        T hv;
+        if constexpr (std::is_same<T, __nv_bfloat16>::value)
+          hv = __float2bfloat16_rn(pv);
+        else
+          hv = __float2half_rn(pv);
+        *reinterpret_cast<T*>(pb + h * 128 + (((tc / 8) ^ (h & 7)) << 4) + (tc % 8) * 2) = hv;
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_ready[t & 1]);
+    }
+    // ------------------------------ epilogue ------------------------------
+    // row sums per head over all 128 token threads (exchange slot n_tiles & 1)
+    if (ok && n_tiles > 0) {
+      float* rb = red + (n_tiles & 1) * 128;
+      const float ws = warp_colreduce16<false>(l_part, lane);
+      if (lane < 16) rb[warp * 16 + lane] = ws;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->red_full[n_tiles & 1]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->red_full[n_tiles & 1], (n_tiles >> 1) & 1, p.ec, abort_flag,
+                                             SITE_DEC_FULL)) &&
+           __all_sync(0xffffffffu, mbar_wait(&bars->o_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, p.ec,
+                                             abort_flag, SITE_DEC_FULL));
+      if (ok) {
+        tc_fence_after();
+        float L[16], inv[16];
+        wg_reduce(rb, L, false);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          inv[j] = L[j] > 0.f ? 1.f / L[j] : 0.f;
+          if (tr == j) {
+            const int64_t pidx = ((int64_t)r * p.max_splits + split) * p.H + 16 * hh + j;
+            p.lse_part[pidx] = L[j] > 0.f ? m_run[j] + lg2(L[j]) : -INFINITY;
+          }
+        }
+#pragma unroll 1
+        for (int m = 0; m < 4; ++m) {
+          uint32_t ov[16];
+          tmem_ld16(tmem + lane_off + 32 * m + 16 * hh, ov);
+          tmem_ld_wait16(ov);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int64_t pidx = ((int64_t)r * p.max_splits + split) * p.H + 16 * hh + j;
+            p.o_part[pidx * MLA_LAT + 128 * m + tr] = __uint_as_float(ov[j]) * inv[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
 }
 
 }  // namespace ffa
@@ -711,9 +918,13 @@ extern "C" int ffa_mla_decode(const void* q, const void* ckv_pages, const int* b
   if (page_size <= 0 || page_size % DEC_CHUNK != 0) return FFA_ERR_UNSUPPORTED;
   if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
   if (chunks_per_split <= 0) chunks_per_split = 32;
-  if ((q_strides[1] % 2) || (q_strides[0] % 2) || (reinterpret_cast<uintptr_t>(q) & 3)) return FFA_ERR_INVALID_ARG;
+  if ((q_strides[1] % 8) || (q_strides[0] % 8) || (reinterpret_cast<uintptr_t>(q) & 15)) return FFA_ERR_INVALID_ARG;
+  if ((o_strides[1] % 4) || (o_strides[0] % 4) || (reinterpret_cast<uintptr_t>(out_lat) & 7)) return FFA_ERR_INVALID_ARG;
   const size_t need = ffa_mla_decode_workspace_size(R, H, max_pages_per_req, page_size, chunks_per_split);
   if (!workspace || workspace_bytes < need) return FFA_ERR_WORKSPACE;
+  // Splits are whole 128-token tiles (8 chunks); rounding up only lowers the
+  // number of splits, so the workspace sized for the caller's value suffices.
+  chunks_per_split = (chunks_per_split + 7) / 8 * 8;
   MlaParams p{};
   p.q = q;
   p.q_sr = q_strides[0];
@@ -737,27 +948,32 @@ extern "C" int ffa_mla_decode(const void* q, const void* ckv_pages, const int* b
   const CUtensorMapDataType dt =
       dtype == FFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uint64_t rows = (uint64_t)num_pages * page_size;
+  // Boxes as tall as a page allows (and dividing the 128-token tile): fewer,
+  // larger TMA requests.
+  int br = 128;
+  while (page_size % br) br /= 2;
+  p.box_rows = br;
   CUtensorMap mc;
   int st = make_tmap_4d(&mc, ckv_pages, dt, 2, MLA_DK, rows, 1, 1, (uint64_t)MLA_DK * 2, rows * MLA_DK * 2,
-                        rows * MLA_DK * 2, 64, DEC_CHUNK);
+                        rows * MLA_DK * 2, 64, br);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto launch = [&](auto kern, auto merge) -> int {
     static bool set_b = false, set_h = false;
     bool& set = (dtype == FFA_DTYPE_BF16) ? set_b : set_h;
     if (!set) {
-      int e = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MLA_SMEM));
+      int e = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MLT_SMEM));
       if (e) return e;
       set = true;
     }
-    kern<<<dim3(p.max_splits, R), DEC_THREADS, MLA_SMEM, s>>>(mc, p);
+    kern<<<dim3(p.max_splits, R), MLT_THREADS, MLT_SMEM, s>>>(mc, p);
     int e = launch_status();
     if (e) return e;
-    merge<<<(R * H * 32 + 255) / 256, 256, 0, s>>>(p.o_part, p.lse_part, ctx_lens, out_lat, lse, R, H, p.max_splits,
-                                                  chunks_per_split, o_strides[0], o_strides[1]);
+    merge<<<R * H, 128, 0, s>>>(p.o_part, p.lse_part, ctx_lens, out_lat, lse, H, p.max_splits, chunks_per_split,
+                                o_strides[0], o_strides[1]);
     return launch_status();
   };
   if (dtype == FFA_DTYPE_BF16)
-    return launch(ffa_mla_decode_kernel<__nv_bfloat16>, ffa_decode_merge_kernel<__nv_bfloat16, MLA_LAT>);
-  return launch(ffa_mla_decode_kernel<__half>, ffa_decode_merge_kernel<__half, MLA_LAT>);
+    return launch(ffa_mla_decode_tc_kernel<__nv_bfloat16>, ffa_mla_merge_kernel<__nv_bfloat16>);
+  return launch(ffa_mla_decode_tc_kernel<__half>, ffa_mla_merge_kernel<__half>);
 }

@@ -26,7 +26,15 @@ from typing import List, Optional, Sequence
 import torch
 
 from . import _lib
-from .decode import default_chunks_per_split
+
+
+def mla_chunks_per_split(ctx_max: int, R: int, num_sms: int = 148) -> int:
+    """16-token chunks per CTA of the latent decode kernel: whole 128-token
+    tiles, and about one CTA per SM (the kernel holds one 147 KB tile in
+    shared memory, so one CTA fits an SM)."""
+    chunks = max(1, math.ceil(ctx_max / 16))
+    splits = max(1, math.ceil(num_sms / max(1, R)))
+    return max(8, math.ceil(math.ceil(chunks / splits) / 8) * 8)
 
 
 def absorbed_weights(mla) -> tuple[torch.Tensor, torch.Tensor]:
@@ -47,7 +55,7 @@ def mla_decode(q: torch.Tensor, ckv_pages: torch.Tensor, block_table: torch.Tens
         raise ValueError("the MLA decode kernel serves latent 512 + rope 64 and 32 heads")
     if q.dtype not in _lib.DTYPE_CODE or ckv_pages.dtype != q.dtype or not ckv_pages.is_contiguous():
         raise ValueError("q / latent cache must share an fp16/bf16 dtype; cache contiguous")
-    if q.stride(-1) != 1:
+    if q.stride(-1) != 1 or q.stride(1) % 8 or q.stride(0) % 8 or q.data_ptr() % 16:
         q = q.contiguous()
     bt = block_table.to(torch.int32).contiguous()
     lens = ctx_lens.to(torch.int32).contiguous()
@@ -55,7 +63,7 @@ def mla_decode(q: torch.Tensor, ckv_pages: torch.Tensor, block_table: torch.Tens
     if chunks_per_split is None:
         ctx_max = max_ctx if max_ctx is not None else max_pages * page_size
         sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-        chunks_per_split = default_chunks_per_split(ctx_max, R, 1, sms)
+        chunks_per_split = mla_chunks_per_split(ctx_max, R, sms)
     out = torch.empty((R, H, 512), dtype=q.dtype, device=q.device)
     lse = torch.empty((R, H), dtype=torch.float32, device=q.device) if return_lse else None
     lib = _lib.load()
