@@ -57,7 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "ffa_bwd": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # dout q k v o lse
         _c_void_p, _c_void_p, _c_void_p,  # dq dk dv
-        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D Dv
         _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p,  # strides q k v o do dq dk dv
         _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream

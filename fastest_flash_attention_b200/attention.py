@@ -23,7 +23,6 @@ from .config import AttentionConfig
 from .utils import auto_select_block_size, maybe_unsqueeze_head
 
 _KERNEL_DTYPES = (torch.float16, torch.bfloat16)
-SUPPORTED_HEAD_DIMS = (64, 128)  # backward
 FWD_HEAD_DIMS = ((64, 64), (128, 128), (192, 128))  # forward (qk, v)
 
 
@@ -189,8 +188,9 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     _lib.require_cuda(dout, q, k, v, o, lse)
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
-    if D not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"head_dim {D} not supported by the sm_100a backward kernel")
+    if (D, v.shape[3]) not in FWD_HEAD_DIMS or o.shape[3] != v.shape[3] or dout.shape[3] != v.shape[3]:
+        raise ValueError(f"head dims (qk={D}, v={v.shape[3]}) not supported by the sm_100a backward kernel "
+                         f"(supported: {FWD_HEAD_DIMS})")
     if Hq % Hkv != 0:
         raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
     dt = kernel_dtype(q, compute_dtype)
@@ -207,7 +207,7 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     with torch.cuda.device(q.device):
         st = lib.ffa_bwd(
             dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D,
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, v.shape[3],
             _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o), _strides_bhs(dout),
             _strides_bhs(dq), _strides_bhs(dk), _strides_bhs(dv),
             float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),

@@ -334,12 +334,9 @@ struct BwdBars {
   int abort;
 };
 
-// TMEM columns: the kept tile as the A operand of the S / dP MMAs, then the
-// score buffers (128 columns each: S or S^T, then dP or dP^T), then the fp32
-// accumulators.  dK/dV needs 256 accumulator columns and so has one score
-// buffer; dQ has two.
-constexpr uint32_t TM_FIXED = 0;    // [0, D/2) first kept operand, [64, 64 + D/2) second (16-bit pairs)
-constexpr uint32_t TM_S = 128;      // score buffer b at [128 + 128 b, 256 + 128 b)
+// TMEM columns (per kernel, in its Cfg): the kept tile as 16-bit A operands
+// of the S / dP MMAs, then the score buffers (128 columns each: S or S^T, then
+// dP or dP^T), then the fp32 accumulators.
 
 __device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns) {
   mbar_init(&bars->fixed_full, 1);
@@ -426,30 +423,41 @@ __device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_st
 // ---------------------------------------------------------------------------
 // 2. dK / dV
 // ---------------------------------------------------------------------------
-template <int D>
+// D = query/key head dim, DV = value head dim.  (D, DV) = (192, 128) is the
+// MLA training shape: its accumulators (dV 128 + dK 192 columns) leave TMEM
+// room for V only, so S^T = K Q^T reads K from smem there.
+template <int D, int DV>
 struct DkdvCfg {
-  static constexpr int TILE = BWD_BT * D * 2;     // K or V tile (128 rows)
-  static constexpr int SUB = BWD_BS * D * 2;      // Q or dO sub-tile (64 rows)
-  static constexpr int NS = D == 64 ? 6 : 3;      // stages of {Q, dO, stats}
+  static constexpr bool K_TMEM = D + DV <= 256;     // K kept in TMEM as an A operand
+  static constexpr uint32_t TM_K = 0;
+  static constexpr uint32_t TM_V = K_TMEM ? 64 : 0;
+  static constexpr uint32_t TM_SC = K_TMEM ? 128 : 64;  // the score buffer (S^T 64 + dP^T 64 columns)
+  static constexpr uint32_t TM_AC = TM_SC + 128;       // dV (DV columns) then dK (D columns)
+  static constexpr int TILE_K = BWD_BT * D * 2;     // K tile (128 rows)
+  static constexpr int TILE_V = BWD_BT * DV * 2;    // V tile
+  static constexpr int SUB_Q = BWD_BS * D * 2;      // Q sub-tile (64 rows)
+  static constexpr int SUB_DO = BWD_BS * DV * 2;    // dO sub-tile
+  static constexpr int STAGE = SUB_Q + SUB_DO;
+  static constexpr int NS = D == 64 ? 6 : (D == 128 ? 3 : 2);  // stages of {Q, dO, stats}
   static constexpr int PT = BWD_BT * BWD_BS * 2;  // one P^T or dS^T tile (128 x 64, 16-bit)
   static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;               // stage s: Q at 2*s*SUB, dO at (2*s+1)*SUB
-  static constexpr int PT_OFF = STAGE_OFF + NS * 2 * SUB;  // pair b: P^T at b*PT, dS^T at (2+b)*PT
+  static constexpr int V_OFF = TILE_K;
+  static constexpr int STAGE_OFF = TILE_K + TILE_V;        // stage s: Q at s*STAGE, dO at s*STAGE + SUB_Q
+  static constexpr int PT_OFF = STAGE_OFF + NS * STAGE;    // pair b: P^T at b*PT, dS^T at (2+b)*PT
   static constexpr int STAT_OFF = PT_OFF + 4 * PT;         // stage s: nlse2[64], delta[64]
   static constexpr int BAR_OFF = STAT_OFF + NS * 2 * BWD_BS * 4;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-template <typename T, int D>
+template <typename T, int D, int DV>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     ffa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                         const BwdParams p) {
-  using Cfg = DkdvCfg<D>;
+  using Cfg = DkdvCfg<D, DV>;
   constexpr int NS = Cfg::NS;
   constexpr int NBUF = 1;
-  constexpr uint32_t TM_ACC = TM_S + 128 * NBUF;
+  constexpr uint32_t TM_ACC = Cfg::TM_AC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + Cfg::K_OFF;
@@ -487,25 +495,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (warp == BWD_WARP_LOAD) {
     if (lane == 0 && n > 0) {
       const uint64_t pol = policy_evict_last();
-      mbar_arrive_expect_tx(&bars->fixed_full, 2 * Cfg::TILE);
-      for (int c = 0; c < D / 64; ++c)
-        for (int hf = 0; hf < 2; ++hf) {
-          const int off = c * BWD_BT * 128 + hf * BWD_BS * 128;
-          tma_load_4d(&tmK, &bars->fixed_full, sK + off, c * 64, j * BWD_BT + hf * BWD_BS, hkv, b, pol);
-          tma_load_4d(&tmV, &bars->fixed_full, sV + off, c * 64, j * BWD_BT + hf * BWD_BS, hkv, b, pol);
-        }
+      mbar_arrive_expect_tx(&bars->fixed_full, Cfg::TILE_K + Cfg::TILE_V);
+      for (int hf = 0; hf < 2; ++hf) {
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(&tmK, &bars->fixed_full, sK + c * BWD_BT * 128 + hf * BWD_BS * 128, c * 64,
+                      j * BWD_BT + hf * BWD_BS, hkv, b, pol);
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_4d(&tmV, &bars->fixed_full, sV + c * BWD_BT * 128 + hf * BWD_BS * 128, c * 64,
+                      j * BWD_BT + hf * BWD_BS, hkv, b, pol);
+      }
       int issued = 0;
       for (int u = 0; u < n; ++u) {
         const int s = u % NS, use = u / NS;
         if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
         const int g = u / n_i, i = i_lo + u % n_i;
         const int h = hkv * group + g;
-        mbar_arrive_expect_tx(&bars->st_full[s], 2 * Cfg::SUB + 2 * BWD_BS * 4);
-        uint8_t* dst = sStage + 2 * s * Cfg::SUB;
-        for (int c = 0; c < D / 64; ++c) {
+        mbar_arrive_expect_tx(&bars->st_full[s], Cfg::STAGE + 2 * BWD_BS * 4);
+        uint8_t* dst = sStage + s * Cfg::STAGE;
+        for (int c = 0; c < D / 64; ++c)
           tma_load_4d(&tmQ, &bars->st_full[s], dst + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
-          tma_load_4d(&tmDO, &bars->st_full[s], dst + Cfg::SUB + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
-        }
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_4d(&tmDO, &bars->st_full[s], dst + Cfg::SUB_Q + c * BWD_BS * 128, c * 64, i * BWD_BS, h, b, pol);
         const int64_t row0 = (int64_t)(b * p.Hq + h) * p.Sq_pad + i * BWD_BS;
         bulk_load(sStat + 2 * BWD_BS * s, p.nlse2 + row0, BWD_BS * 4, &bars->st_full[s]);
         bulk_load(sStat + 2 * BWD_BS * s + BWD_BS, p.delta + row0, BWD_BS * 4, &bars->st_full[s]);
@@ -520,36 +530,43 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (TMEM A x K-major B)
-      const uint32_t idesc_acc = make_idesc_f16(128, D, FMT, 0, 1);     // dV, dK (K-major A x MN-major B)
+      const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (K-major A x K-major B)
+      const uint32_t idesc_dv = make_idesc_f16(128, DV, FMT, 0, 1);     // dV (K-major A x MN-major B)
+      const uint32_t idesc_dk = make_idesc_f16(128, D, FMT, 0, 1);      // dK
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
       const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
       const uint64_t pt_desc = make_sdesc_sw128(smem_u32(sPT), 16, 1024);
-      const uint32_t tK = tmem + TM_FIXED, tV = tmem + TM_FIXED + 64;
-      const uint32_t tS = tmem + TM_S, tDP = tmem + TM_S + 64;
-      const uint32_t tDV = tmem + TM_ACC, tDK = tmem + TM_ACC + D;
+      const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
+      const uint32_t tK = tmem + Cfg::TM_K, tV = tmem + Cfg::TM_V;
+      const uint32_t tS = tmem + Cfg::TM_SC, tDP = tmem + Cfg::TM_SC + 64;
+      const uint32_t tDV = tmem + TM_ACC, tDK = tmem + TM_ACC + DV;
       auto issue_s = [&](int u) {
         const int s = u % NS;
-        const uint64_t q_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
-        const uint64_t do_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint64_t q_k = st_kdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
+        const uint64_t do_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_Q) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tK + 8 * ks, q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          if constexpr (Cfg::K_TMEM)
+            mma_ts(tS, tK + 8 * ks, q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+          else
+            mma_ss(tS, k_desc + kstep(ks, BWD_BT), q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        }
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tDP, tV + 8 * ks, do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tV + 8 * ks, do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
       };
       auto issue_acc = [&](int v) {
         const int bb = v & 1, s = v % NS;
-        const uint64_t q_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
-        const uint64_t do_m = st_mdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint64_t q_m = st_mdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
+        const uint64_t do_m = st_mdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_Q) >> 4);
         const uint64_t p_k = pt_desc + (uint64_t)((bb * Cfg::PT) >> 4);
         const uint64_t ds_k = pt_desc + (uint64_t)(((2 + bb) * Cfg::PT) >> 4);
 #pragma unroll
         for (int ks = 0; ks < BWD_BS / 16; ++ks)
-          mma_ss(tDV, p_k + kstep(ks, BWD_BT), do_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc,
+          mma_ss(tDV, p_k + kstep(ks, BWD_BT), do_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dv,
                  (v > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < BWD_BS / 16; ++ks)
-          mma_ss(tDK, ds_k + kstep(ks, BWD_BT), q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_acc,
+          mma_ss(tDK, ds_k + kstep(ks, BWD_BT), q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dk,
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
@@ -563,13 +580,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;  // key row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + TM_S + 32 * half, tDP = tS + 64;
+    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + 32 * half, tDP = tS + 64;
     const int key = j * BWD_BT + r;
     bool ok = true;
     if (n > 0 && wg < 2) {  // K (warpgroup 0) / V (warpgroup 1) into TMEM as the A operand
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD));
       if (ok) {
-        tile_row_to_tmem<D>(wg == 0 ? sK : sV, r, tmem + lane_off + TM_FIXED + 64 * wg);
+        if (wg == 1)
+          tile_row_to_tmem<DV>(sV, r, tmem + lane_off + Cfg::TM_V);
+        else if (Cfg::K_TMEM)
+          tile_row_to_tmem<D>(sK, r, tmem + lane_off + Cfg::TM_K);
         tmem_st_wait();
         tc_fence_before();
       }
@@ -604,10 +624,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     T* row = pair == 0
                  ? reinterpret_cast<T*>(p.dv) + (size_t)b * p.dv_sb + (size_t)hkv * p.dv_sh + (size_t)key * p.dv_ss
                  : reinterpret_cast<T*>(p.dk) + (size_t)b * p.dk_sb + (size_t)hkv * p.dk_sh + (size_t)key * p.dk_ss;
-    const uint32_t tacc = tmem + lane_off + TM_ACC + pair * D;
+    const uint32_t tacc = tmem + lane_off + TM_ACC + pair * DV;
     const float mul = pair ? p.scale : 1.f;
-#pragma unroll
-    for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
+    const int ncol = pair ? D : DV;
+#pragma unroll 1
+    for (int c = half * (ncol / 2); c < (half + 1) * (ncol / 2); c += 32) {
       uint32_t v[32];
       if (have) {
         tmem_ld32(tacc + c, v);
@@ -630,29 +651,39 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // ---------------------------------------------------------------------------
 // 3. dQ
 // ---------------------------------------------------------------------------
-template <int D>
+// (D, DV) = (192, 128): Q and dO (160 packed columns) and dQ (192) leave TMEM
+// room for one score buffer.
+template <int D, int DV>
 struct DqCfg {
-  static constexpr int TILE = BWD_BT * D * 2;     // Q or dO tile (128 rows)
-  static constexpr int SUB = BWD_BS * D * 2;      // K or V sub-tile (64 rows)
-  static constexpr int NS = D == 64 ? 8 : 4;      // stages of {K, V}
+  static constexpr int NBUF = D <= 128 ? 2 : 1;
+  static constexpr uint32_t TM_Q = 0;
+  static constexpr uint32_t TM_DO = D <= 128 ? 64 : D / 2;
+  static constexpr uint32_t TM_SC = D <= 128 ? 128 : 160;  // score buffer b at TM_SC + 128 b
+  static constexpr uint32_t TM_AC = TM_SC + 128 * NBUF;    // dQ (D columns)
+  static constexpr int TILE_Q = BWD_BT * D * 2;     // Q tile (128 rows)
+  static constexpr int TILE_DO = BWD_BT * DV * 2;   // dO tile
+  static constexpr int SUB_K = BWD_BS * D * 2;      // K sub-tile (64 rows)
+  static constexpr int SUB_V = BWD_BS * DV * 2;     // V sub-tile
+  static constexpr int STAGE = SUB_K + SUB_V;
+  static constexpr int NS = D == 64 ? 8 : (D == 128 ? 4 : 2);  // stages of {K, V}
   static constexpr int DS = BWD_BT * BWD_BS * 2;  // one dS tile (128 x 64, 16-bit)
   static constexpr int Q_OFF = 0;
-  static constexpr int DO_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;               // stage s: K at 2*s*SUB, V at (2*s+1)*SUB
-  static constexpr int DS_OFF = STAGE_OFF + NS * 2 * SUB;  // pair b: dS at b*DS
+  static constexpr int DO_OFF = TILE_Q;
+  static constexpr int STAGE_OFF = TILE_Q + TILE_DO;     // stage s: K at s*STAGE, V at s*STAGE + SUB_K
+  static constexpr int DS_OFF = STAGE_OFF + NS * STAGE;  // pair b: dS at b*DS
   static constexpr int BAR_OFF = DS_OFF + 2 * DS;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-template <typename T, int D>
+template <typename T, int D, int DV>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                       const BwdParams p) {
-  using Cfg = DqCfg<D>;
+  using Cfg = DqCfg<D, DV>;
   constexpr int NS = Cfg::NS;
-  constexpr int NBUF = 2;
-  constexpr uint32_t TM_ACC = TM_S + 128 * NBUF;
+  constexpr int NBUF = Cfg::NBUF;
+  constexpr uint32_t TM_ACC = Cfg::TM_AC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
@@ -690,24 +721,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     if (lane == 0 && n > 0) {
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_last();
-      mbar_arrive_expect_tx(&bars->fixed_full, 2 * Cfg::TILE);
-      for (int c = 0; c < D / 64; ++c)
-        for (int hf = 0; hf < 2; ++hf) {
-          const int off = c * BWD_BT * 128 + hf * BWD_BS * 128;
-          tma_load_4d(&tmQ, &bars->fixed_full, sQ + off, c * 64, i * BWD_BT + hf * BWD_BS, h, b, pol_q);
-          tma_load_4d(&tmDO, &bars->fixed_full, sDO + off, c * 64, i * BWD_BT + hf * BWD_BS, h, b, pol_q);
-        }
+      mbar_arrive_expect_tx(&bars->fixed_full, Cfg::TILE_Q + Cfg::TILE_DO);
+      for (int hf = 0; hf < 2; ++hf) {
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(&tmQ, &bars->fixed_full, sQ + c * BWD_BT * 128 + hf * BWD_BS * 128, c * 64,
+                      i * BWD_BT + hf * BWD_BS, h, b, pol_q);
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_4d(&tmDO, &bars->fixed_full, sDO + c * BWD_BT * 128 + hf * BWD_BS * 128, c * 64,
+                      i * BWD_BT + hf * BWD_BS, h, b, pol_q);
+      }
       int issued = 0;
       for (int u = 0; u < n; ++u) {
         const int s = u % NS, use = u / NS;
         if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
         const int jj = j_lo + u;
-        mbar_arrive_expect_tx(&bars->st_full[s], 2 * Cfg::SUB);
-        uint8_t* dst = sStage + 2 * s * Cfg::SUB;
-        for (int c = 0; c < D / 64; ++c) {
+        mbar_arrive_expect_tx(&bars->st_full[s], Cfg::STAGE);
+        uint8_t* dst = sStage + s * Cfg::STAGE;
+        for (int c = 0; c < D / 64; ++c)
           tma_load_4d(&tmK, &bars->st_full[s], dst + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b, pol_kv);
-          tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b, pol_kv);
-        }
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB_K + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b,
+                      pol_kv);
         ++issued;
       }
       if (*abort_flag) {
@@ -724,21 +758,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
       const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
       const uint64_t ds_desc = make_sdesc_sw128(smem_u32(sDS), 16, 1024);
-      const uint32_t tQ = tmem + TM_FIXED, tDO = tmem + TM_FIXED + 64;
+      const uint32_t tQ = tmem + Cfg::TM_Q, tDO = tmem + Cfg::TM_DO;
       const uint32_t tDQ = tmem + TM_ACC;
       auto issue_s = [&](int u) {
         const int s = u % NS;
-        const uint32_t tS = tmem + TM_S + 128 * (u % NBUF), tDP = tS + 64;
-        const uint64_t k_k = st_kdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
-        const uint64_t v_k = st_kdesc + (uint64_t)(((2 * s + 1) * Cfg::SUB) >> 4);
+        const uint32_t tS = tmem + Cfg::TM_SC + 128 * (u % NBUF), tDP = tS + 64;
+        const uint64_t k_k = st_kdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
+        const uint64_t v_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_K) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+        for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
       };
       auto issue_acc = [&](int v) {
         const int bb = v & 1, s = v % NS;
-        const uint64_t k_m = st_mdesc + (uint64_t)((2 * s * Cfg::SUB) >> 4);
+        const uint64_t k_m = st_mdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
         const uint64_t ds_k = ds_desc + (uint64_t)((bb * Cfg::DS) >> 4);
 #pragma unroll
         for (int ks = 0; ks < BWD_BS / 16; ++ks)
@@ -756,7 +790,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + TM_S + 128 * (pair % NBUF) + 32 * half, tDP = tS + 64;
+    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + 128 * (pair % NBUF) + 32 * half, tDP = tS + 64;
     const int row = i * BWD_BT + r;
     const int q_abs = row + p.q_offset;
     const int64_t sidx = (int64_t)(b * p.Hq + h) * p.Sq_pad + row;
@@ -765,7 +799,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     if (n > 0 && wg < 2) {  // Q (warpgroup 0) / dO (warpgroup 1) into TMEM as the A operand
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD));
       if (ok) {
-        tile_row_to_tmem<D>(wg == 0 ? sQ : sDO, r, tmem + lane_off + TM_FIXED + 64 * wg);
+        if (wg == 0)
+          tile_row_to_tmem<D>(sQ, r, tmem + lane_off + Cfg::TM_Q);
+        else
+          tile_row_to_tmem<DV>(sDO, r, tmem + lane_off + Cfg::TM_DO);
         tmem_st_wait();
         tc_fence_before();
       }
@@ -820,7 +857,7 @@ static int set_smem(K kern, int bytes) {
   return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 
-template <typename T, int D>
+template <typename T, int D, int DV>
 static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o, const void* dout,
                       const float* lse, float* lse2, float* delta, const int64_t* o_str, const int64_t* do_str,
                       cudaStream_t st) {
@@ -829,32 +866,32 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
   const int threads = 256;
   const int blocks = (n_rows * 32 + threads - 1) / threads;
   ffa_bwd_pre_kernel<T><<<blocks, threads, 0, st>>>(
-      reinterpret_cast<const T*>(o), reinterpret_cast<const T*>(dout), lse, lse2, delta, p.Hq, p.Sq, p.Sq_pad, D,
+      reinterpret_cast<const T*>(o), reinterpret_cast<const T*>(dout), lse, lse2, delta, p.Hq, p.Sq, p.Sq_pad, DV,
       o_str[0], o_str[1], o_str[2], do_str[0], do_str[1], do_str[2], n_rows);
   int s = launch_status();
   if (s) return s;
   // 2. dK / dV
   {
-    auto kern = ffa_bwd_dkdv_kernel<T, D>;
+    auto kern = ffa_bwd_dkdv_kernel<T, D, DV>;
     static bool set = false;
     if (!set) {
-      if ((s = set_smem(kern, DkdvCfg<D>::SMEM))) return s;
+      if ((s = set_smem(kern, DkdvCfg<D, DV>::SMEM))) return s;
       set = true;
     }
     const int grid = (p.Skv + BWD_BT - 1) / BWD_BT * p.B * p.Hkv;
-    kern<<<grid, BWD_THREADS, DkdvCfg<D>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
+    kern<<<grid, BWD_THREADS, DkdvCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;
   }
   // 3. dQ
   {
-    auto kern = ffa_bwd_dq_kernel<T, D>;
+    auto kern = ffa_bwd_dq_kernel<T, D, DV>;
     static bool set = false;
     if (!set) {
-      if ((s = set_smem(kern, DqCfg<D>::SMEM))) return s;
+      if ((s = set_smem(kern, DqCfg<D, DV>::SMEM))) return s;
       set = true;
     }
     const int grid = (p.Sq + BWD_BT - 1) / BWD_BT * p.B * p.Hq;
-    kern<<<grid, BWD_THREADS, DqCfg<D>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
+    kern<<<grid, BWD_THREADS, DqCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;
   }
   return FFA_OK;
@@ -869,7 +906,7 @@ extern "C" size_t ffa_bwd_workspace_size(int B, int Hq, int Sq) {
 
 extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o,
                        const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq,
-                       int Skv, int D, const int64_t* q_strides, const int64_t* k_strides,
+                       int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
                        const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
                        const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
                        float scale, int causal, int q_offset, int window, float softcap, void* workspace,
@@ -880,7 +917,7 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
       !dv_strides)
     return FFA_ERR_INVALID_ARG;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0 || Hq % Hkv != 0) return FFA_ERR_INVALID_ARG;
-  if (D != 64 && D != 128) return FFA_ERR_UNSUPPORTED;
+  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128))) return FFA_ERR_UNSUPPORTED;
   if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
   const size_t need = ffa_bwd_workspace_size(B, Hq, Sq);
   if (!workspace || workspace_bytes < need) return FFA_ERR_WORKSPACE;
@@ -936,17 +973,20 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
     st = make_tmap_4d(&maps[1], k, dt, 2, D, Skv, Hkv, B, k_strides[2] * 2, k_strides[1] * 2, k_strides[0] * 2, 64,
                       BWD_BS);
   if (!st)
-    st = make_tmap_4d(&maps[2], v, dt, 2, D, Skv, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
+    st = make_tmap_4d(&maps[2], v, dt, 2, Dv, Skv, Hkv, B, v_strides[2] * 2, v_strides[1] * 2, v_strides[0] * 2, 64,
                       BWD_BS);
   if (!st)
-    st = make_tmap_4d(&maps[3], dout, dt, 2, D, Sq, Hq, B, do_strides[2] * 2, do_strides[1] * 2, do_strides[0] * 2,
+    st = make_tmap_4d(&maps[3], dout, dt, 2, Dv, Sq, Hq, B, do_strides[2] * 2, do_strides[1] * 2, do_strides[0] * 2,
                       64, BWD_BS);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FFA_DTYPE_BF16) {
-    if (D == 64) return launch_bwd<__nv_bfloat16, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-    return launch_bwd<__nv_bfloat16, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+    if (D == 64) return launch_bwd<__nv_bfloat16, 64, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+    if (D == 128)
+      return launch_bwd<__nv_bfloat16, 128, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+    return launch_bwd<__nv_bfloat16, 192, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
   }
-  if (D == 64) return launch_bwd<__half, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-  return launch_bwd<__half, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+  if (D == 64) return launch_bwd<__half, 64, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+  if (D == 128) return launch_bwd<__half, 128, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+  return launch_bwd<__half, 192, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
 }

@@ -78,7 +78,7 @@ extern "C" int ffa_bwd_noalloc(const void* dout, const void* q, const void* k, c
   void* scratch = nullptr;
   int st = scratch_address(&scratch);
   if (st) return st;
-  return ffa_bwd(dout, q, k, v, o, lse, dq, dk, dv, dtype, B, Hq, Hkv, Sq, Skv, D, q_strides, k_strides, v_strides,
+  return ffa_bwd(dout, q, k, v, o, lse, dq, dk, dv, dtype, B, Hq, Hkv, Sq, Skv, D, D, q_strides, k_strides, v_strides,
                  o_strides, do_strides, dq_strides, dk_strides, dv_strides, scale, causal, q_offset, window, softcap,
                  scratch, BWD_NOALLOC_BYTES, dev_err, stream);
 }

@@ -86,8 +86,10 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
  * results run to run).  Replaces ops/attention_backward.py:19
  * fastest_flash_attn_backward -> kernels/cpu_reference.py:319 and
  * kernels/cpu_fa4.py:445.
- *   dout, o [B, Hq, Sq, D]; lse [B, Hq, Sq] fp32 (natural log, from ffa_fwd)
- *   dq [B, Hq, Sq, D]; dk, dv [B, Hkv, Skv, D] (GQA groups summed in order)
+ *   q, dq [B, Hq, Sq, D]; k, dk [B, Hkv, Skv, D]; v, dv [B, Hkv, Skv, Dv]
+ *   dout, o [B, Hq, Sq, Dv]; lse [B, Hq, Sq] fp32 (natural log, from ffa_fwd)
+ *   (GQA groups summed in order into dk / dv).  (D, Dv) in {(64, 64),
+ *   (128, 128), (192, 128)}; the last is the MLA training shape.
  * Same mask / softcap semantics as ffa_fwd (no block mask: the reference
  * backward has none).  `workspace` must hold ffa_bwd_workspace_size() bytes
  * of device memory (padded base-2 LSE and Delta = rowsum(dO*O)).
@@ -96,7 +98,7 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
 size_t ffa_bwd_workspace_size(int B, int Hq, int Sq);
 
 int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
-            void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq, int Skv, int D,
+            void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq, int Skv, int D, int Dv,
             const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
             const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
             const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,

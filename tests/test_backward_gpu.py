@@ -95,6 +95,25 @@ def test_backward_vs_oracle(B, Hq, Hkv, S, D, causal, window, softcap):
         assert e <= G_TOL, f"{nm}: rel err {e:.3e}"
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,S,causal", [
+    (1, 4, 4, 300, True),    # ragged, causal
+    (2, 4, 2, 256, False),   # GQA
+])
+def test_backward_mla_shape_vs_oracle(B, Hq, Hkv, S, causal):
+    """qk head dim 192 (128 + 64 rotary), value head dim 128: the MLA training shape."""
+    q, k, v, do = _rand(B, Hq, S, 192, seed=11), _rand(B, Hkv, S, 192, seed=12), _rand(B, Hkv, S, 128, seed=13), \
+        _rand(B, Hq, S, 128, seed=14)
+    qc, kc, vc = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = ffa().fastest_flash_attn_func(qc, kc, vc, scale=192 ** -0.5, causal=causal)
+    assert o.shape[-1] == 128
+    o.backward(do.cuda())
+    rdq, rdk, rdv = _oracle_grads(q, k, v, do, Hq, causal=causal, scale=192 ** -0.5)
+    for t, ref, nm in ((qc, rdq, "dq"), (kc, rdk, "dk"), (vc, rdv, "dv")):
+        assert t.grad.shape == t.shape
+        e = rel_err(t.grad, ref)
+        assert e <= G_TOL, f"{nm}: rel err {e:.3e}"
+
+
 def test_config1_fp32_full():
     """Config 1 at full size: fp32 [2,8,1024,64], causal, loss = out.sum()."""
     q, k, v = (_rand(2, 8, 1024, 64, seed=s, dtype=torch.float32) for s in (5, 6, 7))

@@ -112,3 +112,34 @@ def test_mla_absorbed_decode_matches_full_recompute():
         y = dec.step(xs[:, s:s + 1], [0, 1])
         ref = _mla_oracle(mod, xs[:, :s + 1])[:, -1:]
         assert rel(y, ref) <= 3e-2, s
+
+
+def test_mla_module_training_backward():
+    """FastestFlashMLA in training mode: forward + backward through the
+    (qk 192, v 128) kernels, against the same module computed by a plain fp32
+    torch attention."""
+    m = ffa()
+    torch.manual_seed(4)
+    mod = m.FastestFlashMLA(hidden_size=256, num_heads=4, head_dim=128, latent_dim=128, rope_dim=64).cuda().train()
+    for prm in mod.parameters():
+        torch.nn.init.normal_(prm, std=0.05)
+    x = torch.randn(2, 150, 256, device="cuda", requires_grad=True)
+    y = mod(x)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    gx = x.grad.clone()
+    gw = mod.q_proj.weight.grad.clone()
+    # reference: identical projections, attention in fp32 torch
+    x2 = x.detach().clone().requires_grad_(True)
+    mod.zero_grad()
+    q, k, v = mod.qkv(x2)
+    s = (q.float() @ k.float().transpose(-1, -2)) * mod.scale
+    S = s.shape[-1]
+    s = s.masked_fill(torch.ones(S, S, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    o = torch.softmax(s, -1) @ v.float()
+    o = torch.nn.functional.pad(o, (0, mod.rope_dim)).to(x2.dtype)
+    y2 = mod.o_proj(o.transpose(1, 2).reshape(2, 150, -1))
+    y2.backward(gy)
+    assert rel(y, y2.detach().float().cpu().numpy()) <= 3e-2
+    assert rel(gx, x2.grad.float().cpu().numpy()) <= 5e-2
+    assert rel(gw, mod.q_proj.weight.grad.float().cpu().numpy()) <= 5e-2
