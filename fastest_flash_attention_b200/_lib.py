@@ -86,6 +86,10 @@ SIGNATURES: dict[str, tuple] = {
         _c_i64p, _c_i64p, _c_float, _c_int,  # q_strides o_strides scale chunks_per_split
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
     ]),
+    "ffa_merge_partial": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # o_acc lse_acc o_part lse_part
+        _c_int, ctypes.c_int64, _c_int, _c_void_p,  # dtype rows D stream
+    ]),
     "ffa_paged_append": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # k_new v_new k_pages v_pages slots
         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype n_tokens Hkv D page_size num_pages

@@ -180,6 +180,18 @@ int ffa_paged_append(const void* k_new, const void* v_new, void* k_pages, void* 
                      int dtype, int n_tokens, int Hkv, int D, int page_size, int num_pages,
                      const int64_t* new_strides, void* stream);
 
+/* ----------------------------------------------------------------------------
+ * Log-sum-exp merge of a partial attention result into a running one, for
+ * the sequence-sharded ring (each step attends the local queries to one
+ * rank's K/V block; the reference has no multi-GPU path, so this has no
+ * counterpart there).  In place on (o_acc, lse_acc):
+ *   L = logaddexp(L_acc, L_part);  O_acc = O_acc e^(L_acc-L) + O_part e^(L_part-L)
+ *   o_acc [rows, D] fp32, lse_acc [rows] fp32 natural log (-inf = empty)
+ *   o_part [rows, D] dtype (f16/bf16), lse_part [rows] fp32 natural log
+ * ------------------------------------------------------------------------- */
+int ffa_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int dtype,
+                      int64_t rows, int D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
