@@ -23,6 +23,13 @@
 #include "ffa_host.h"
 
 namespace ffa {
+// The MMA issuer's wait: a non-blocking probe first (cheap when the phase is
+// already complete, the common case), then the bounded blocking wait.
+__device__ __forceinline__ bool mbar_wait_mma(uint64_t* bar, uint32_t parity, const ErrCtx& ec, volatile int* abort,
+                                              uint32_t site, bool drain = false) {
+  if (mbar_poll(bar, parity)) return true;
+  return mbar_wait(bar, parity, ec, abort, site, drain);
+}
 
 constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
 constexpr int FWD_NQT = 2;    // query tiles per CTA
@@ -35,7 +42,11 @@ constexpr int FWD_WARP_LOAD = 8;
 constexpr int FWD_WARP_MMA = 9;
 constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block mask filters them
 constexpr float RESCALE_LOG2 = 8.0f;
-constexpr int FWD_PCH = 4;  // P is handed to the MMA warp in 4 chunks of 32 keys
+#ifndef FFA_FWD_PCH
+#define FFA_FWD_PCH 2
+#endif
+constexpr int FWD_PCH = FFA_FWD_PCH;  // P is handed to the MMA warp in FWD_PCH chunks of 128 / FWD_PCH keys (2: each
+// hand-over costs the MMA warp a barrier wait, and fewer waits measured faster)
 
 // D = query/key head dim, DV = value head dim (DV <= 128; D = 192 with
 // DV = 128 is the MLA prefill shape: 128 "nope" + 64 rotary dims).
@@ -276,9 +287,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           mma_ts(d, a + ks * 8, vb + (uint64_t)((ks * 16 * 128) >> 4), idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
       };
-      bool ok = n == 0 || mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_Q);
+      bool ok = n == 0 || mbar_wait_mma(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_Q);
       if (ok && n > 0) {
-        ok = mbar_wait(&bars->kv_full[0], 0, p.ec, abort_flag, SITE_FWD_KV_FULL);
+        ok = mbar_wait_mma(&bars->kv_full[0], 0, p.ec, abort_flag, SITE_FWD_KV_FULL);
         if (ok) {
           tc_fence_after();
           issue_qk(0, 0);
@@ -292,10 +303,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         const int vs = 2 * it + 1, vb = vs % Cfg::NBUF;
         const bool has_next = it + 1 < n;
         const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
-        if (!mbar_wait(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
+        if (!mbar_wait_mma(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
         for (int t = 0; t < FWD_NQT && ok; ++t) {
           for (int k = 0; k < FWD_PCH; ++k) {
-            if (!mbar_wait(&bars->p_full[t][k], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
+            if (!mbar_wait_mma(&bars->p_full[t][k], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
               ok = false;
               break;
             }
@@ -305,7 +316,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           if (!ok) break;
           mma_commit(&bars->o_done[t]);
           if (has_next) {
-            if (t == 0 && !mbar_wait(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
+            if (t == 0 && !mbar_wait_mma(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
               ok = false;
               break;
             }
@@ -320,7 +331,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       }
       // Every MMA must retire before TMEM is released.
       mma_commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+      mbar_wait_mma(&bars->drain, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
     }
     __syncwarp();
    }
@@ -455,19 +466,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int k = 0; k < FWD_PCH; ++k) {
-        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int c = k * 16 + e;
-          const float2 a =
-              ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), mul2, nmu2);
-          float2 pv;
-          pv.x = ex2(a.x);
-          pv.y = ex2(a.y);
-          acc[e & 3] = fadd2(acc[e & 3], pv);
-          pk[e] = pack2<T>(pv.x, pv.y);
+        for (int g = 0; g < 4 / FWD_PCH; ++g) {  // 16 packed pairs (32 keys) per group
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int c = (k * (4 / FWD_PCH) + g) * 16 + e;
+            const float2 a =
+                ffma2(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), mul2, nmu2);
+            float2 pv;
+            pv.x = ex2(a.x);
+            pv.y = ex2(a.y);
+            acc[e & 3] = fadd2(acc[e & 3], pv);
+            pk[e] = pack2<T>(pv.x, pv.y);
+          }
+          tmem_st16(tS + (k * (4 / FWD_PCH) + g) * 16, pk);
         }
-        tmem_st16(tS + k * 16, pk);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
