@@ -13,22 +13,25 @@
 //        P^T = 2^(S^T*scale*log2e + NLSE2), dS^T = P^T (dP^T - Delta) [* softcap']
 //        dV += P^T dO,  dK += dS^T Q      (P^T / dS^T as 16-bit A operands in TMEM)
 //   3. dQ: one CTA per (batch, query head, 128-row query tile), streaming
-//      64-key sub-tiles:  S = Q K^T, dP = dO V^T, dS as above, dQ += dS K.
-// Both main kernels double-buffer the score tiles in TMEM: alternate sub-tiles
-// go to alternate buffers.  A compute warpgroup loads its S / dP columns into
+//      key units (128 keys for D <= 128, 64 for D = 192):
+//        S = Q K^T, dP = dO V^T, dS as above, dQ += dS K.
+// The dK/dV kernel double-buffers the score tiles in TMEM (alternate sub-tiles
+// go to alternate buffers); the dQ kernel has one buffer of a wider unit.  A compute warpgroup loads its S / dP columns into
 // registers and releases the TMEM buffer at once, then writes the 16-bit P^T /
 // dS tiles to shared memory (128-byte swizzled, K-major: the A operands of the
 // accumulation MMAs).  So the next S / dP MMAs into a buffer never wait for
 // the accumulation MMAs of the sub-tile before, and the tensor core runs
 // S(u+1), dV/dK(u) while unit u+1's compute overlaps them.
-//   warps 0-15  compute warpgroups 0-3: warpgroup w serves buffer w % 2 and
-//               columns [32 (w / 2), 32 (w / 2) + 32) of its 64-column
-//               sub-tile; one TMEM lane = one row
+//   warps 0-15  compute warpgroups 0-3.  dK/dV (and dQ at D = 192):
+//               warpgroup w serves alternate units (w % 2) and columns
+//               [32 (w / 2), 32 (w / 2) + 32) of a 64-column sub-tile.  dQ at
+//               D <= 128: every warpgroup serves every 128-key unit, columns
+//               [32 w, 32 w + 32).  One TMEM lane = one row.
 //   warp 16     TMA producer
 //   warp 17     MMA issuer, TMEM owner
 // dK and dQ are multiplied by the softmax scale in their epilogues.
-// TMEM (both kernels): buffer b at columns [128b, 128b+64) scores (S or S^T),
-// [128b+64, 128b+128) dP; accumulators from 256.
+// TMEM: the kept tile (16-bit A operands), then the score buffers (S or S^T,
+// then dP or dP^T), then the fp32 accumulators; offsets in DkdvCfg / DqCfg.
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
@@ -338,7 +341,8 @@ struct BwdBars {
 // of the S / dP MMAs, then the score buffers (128 columns each: S or S^T, then
 // dP or dP^T), then the fp32 accumulators.
 
-__device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns) {
+// `consumers`: warps that read each unit's scores and store its P / dS.
+__device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns, int consumers) {
   mbar_init(&bars->fixed_full, 1);
   mbar_init(&bars->fixed_tmem, 2 * 4);
   for (int s = 0; s < ns; ++s) {
@@ -347,8 +351,8 @@ __device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns) {
   }
   for (int t = 0; t < 2; ++t) {
     mbar_init(&bars->sp_full[t], 1);
-    mbar_init(&bars->tmem_free[t], 2 * 4);
-    mbar_init(&bars->ds_ready[t], 2 * 4);
+    mbar_init(&bars->tmem_free[t], consumers);
+    mbar_init(&bars->ds_ready[t], consumers);
     mbar_init(&bars->pt_free[t], 1);
   }
   mbar_init(&bars->acc_done, 1);
@@ -482,7 +486,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int n = n_i * group;  // units: (query head of the group, 64-row query sub-tile), head-major
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (threadIdx.x == 0) bwd_init_bars(bars, NS);
+  if (threadIdx.x == 0) bwd_init_bars(bars, NS, 2 * 4);
   if (warp == BWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -653,25 +657,36 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // ---------------------------------------------------------------------------
 // (D, DV) = (192, 128): Q and dO (160 packed columns) and dQ (192) leave TMEM
 // room for one score buffer.
+// A unit is UK keys.  D <= 128: UK = 128; the TMEM (Q 16-bit + dO 16-bit,
+// one score buffer S 128 + dP 128 columns, dQ) holds exactly one score buffer,
+// and all four compute warpgroups share each unit, 32 columns each.  The two
+// dS tiles (128 x 128) reuse the smem of Q / dO once those are in TMEM.
+// D = 192: UK = 64 with one score buffer; the warpgroup pairs alternate units.
 template <int D, int DV>
 struct DqCfg {
-  static constexpr int NBUF = D <= 128 ? 2 : 1;
+  static constexpr int UK = D <= 128 ? 128 : 64;
+  static constexpr bool WIDE = UK == 128;
+  static constexpr int NBUF = 1;
   static constexpr uint32_t TM_Q = 0;
   static constexpr uint32_t TM_DO = D <= 128 ? 64 : D / 2;
-  static constexpr uint32_t TM_SC = D <= 128 ? 128 : 160;  // score buffer b at TM_SC + 128 b
-  static constexpr uint32_t TM_AC = TM_SC + 128 * NBUF;    // dQ (D columns)
+  static constexpr uint32_t TM_SC = D <= 128 ? 128 : 160;  // S at TM_SC, dP at TM_SC + UK
+  static constexpr uint32_t TM_AC = TM_SC + 2 * UK * NBUF; // dQ (D columns)
+  static_assert(TM_AC + D <= 512, "dQ TMEM budget");
   static constexpr int TILE_Q = BWD_BT * D * 2;     // Q tile (128 rows)
   static constexpr int TILE_DO = BWD_BT * DV * 2;   // dO tile
-  static constexpr int SUB_K = BWD_BS * D * 2;      // K sub-tile (64 rows)
-  static constexpr int SUB_V = BWD_BS * DV * 2;     // V sub-tile
+  static constexpr int SUB_K = UK * D * 2;          // K sub-tile (UK rows)
+  static constexpr int SUB_V = UK * DV * 2;         // V sub-tile
   static constexpr int STAGE = SUB_K + SUB_V;
-  static constexpr int NS = D == 64 ? 8 : (D == 128 ? 4 : 2);  // stages of {K, V}
-  static constexpr int DS = BWD_BT * BWD_BS * 2;  // one dS tile (128 x 64, 16-bit)
+  static constexpr int DS = BWD_BT * UK * 2;        // one dS tile (128 x UK, 16-bit)
+  static constexpr bool DS_ALIAS = 2 * DS <= TILE_Q + TILE_DO;  // dS tiles over Q / dO
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = TILE_Q;
-  static constexpr int STAGE_OFF = TILE_Q + TILE_DO;     // stage s: K at s*STAGE, V at s*STAGE + SUB_K
-  static constexpr int DS_OFF = STAGE_OFF + NS * STAGE;  // pair b: dS at b*DS
-  static constexpr int BAR_OFF = DS_OFF + 2 * DS;
+  static constexpr int STAGE_OFF = TILE_Q + TILE_DO + (DS_ALIAS ? 0 : 2 * DS);
+  static constexpr int DS_OFF = DS_ALIAS ? 0 : TILE_Q + TILE_DO;  // tile b at b*DS
+  static constexpr int NS = (227 * 1024 - 256 - 1024 - STAGE_OFF) / STAGE > 8 ? 8
+                            : (227 * 1024 - 256 - 1024 - STAGE_OFF) / STAGE;  // stages of {K, V}
+  static_assert(NS >= 2, "dQ smem budget");
+  static constexpr int BAR_OFF = STAGE_OFF + NS * STAGE;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
@@ -683,6 +698,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   using Cfg = DqCfg<D, DV>;
   constexpr int NS = Cfg::NS;
   constexpr int NBUF = Cfg::NBUF;
+  constexpr int UK = Cfg::UK;
   constexpr uint32_t TM_ACC = Cfg::TM_AC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -704,10 +720,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int hkv = h / (p.Hq / p.Hkv);
   int j_lo, j_hi;
   k_range_for_q_tile(p, i, j_lo, j_hi);
-  const int n = max(0, j_hi - j_lo);  // units: 64-key sub-tiles
+  // units of UK keys covering the 64-key sub-tiles [j_lo, j_hi); keys of a
+  // unit outside the row's range are masked per column
+  constexpr int R = UK / BWD_BS;
+  j_lo = j_lo / R;
+  j_hi = (j_hi + R - 1) / R;
+  const int n = max(0, j_hi - j_lo);
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (threadIdx.x == 0) bwd_init_bars(bars, NS);
+  if (threadIdx.x == 0) bwd_init_bars(bars, NS, Cfg::WIDE ? 4 * 4 : 2 * 4);
   if (warp == BWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -737,11 +758,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const int jj = j_lo + u;
         mbar_arrive_expect_tx(&bars->st_full[s], Cfg::STAGE);
         uint8_t* dst = sStage + s * Cfg::STAGE;
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(&tmK, &bars->st_full[s], dst + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b, pol_kv);
-        for (int c = 0; c < DV / 64; ++c)
-          tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB_K + c * BWD_BS * 128, c * 64, jj * BWD_BS, hkv, b,
-                      pol_kv);
+        for (int hf = 0; hf < R; ++hf) {
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(&tmK, &bars->st_full[s], dst + c * UK * 128 + hf * BWD_BS * 128, c * 64,
+                        jj * UK + hf * BWD_BS, hkv, b, pol_kv);
+          for (int c = 0; c < DV / 64; ++c)
+            tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB_K + c * UK * 128 + hf * BWD_BS * 128, c * 64,
+                        jj * UK + hf * BWD_BS, hkv, b, pol_kv);
+        }
         ++issued;
       }
       if (*abort_flag) {
@@ -753,29 +777,29 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     __syncwarp();
   } else if (warp == BWD_WARP_MMA) {
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_s = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S, dP (TMEM A x K-major B)
-      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);     // dQ (K-major A x MN-major B)
+      const uint32_t idesc_s = make_idesc_f16(128, UK, FMT, 0, 0);  // S, dP (TMEM A x K-major B)
+      const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);  // dQ (K-major A x MN-major B)
       const uint64_t st_kdesc = make_sdesc_sw128(smem_u32(sStage), 16, 1024);
-      const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
+      const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), UK * 128, 1024);
       const uint64_t ds_desc = make_sdesc_sw128(smem_u32(sDS), 16, 1024);
       const uint32_t tQ = tmem + Cfg::TM_Q, tDO = tmem + Cfg::TM_DO;
       const uint32_t tDQ = tmem + TM_ACC;
       auto issue_s = [&](int u) {
         const int s = u % NS;
-        const uint32_t tS = tmem + Cfg::TM_SC + 128 * (u % NBUF), tDP = tS + 64;
+        const uint32_t tS = tmem + Cfg::TM_SC + 2 * UK * (u % NBUF), tDP = tS + UK;
         const uint64_t k_k = st_kdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
         const uint64_t v_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_K) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+        for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, UK), idesc_s, ks > 0);
 #pragma unroll
-        for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, BWD_BS), idesc_s, ks > 0);
+        for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, UK), idesc_s, ks > 0);
       };
       auto issue_acc = [&](int v) {
         const int bb = v & 1, s = v % NS;
         const uint64_t k_m = st_mdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
         const uint64_t ds_k = ds_desc + (uint64_t)((bb * Cfg::DS) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < BWD_BS / 16; ++ks)
+        for (int ks = 0; ks < UK / 16; ++ks)
           mma_ss(tDQ, ds_k + kstep(ks, BWD_BT), k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq,
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
@@ -790,7 +814,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + 128 * (pair % NBUF) + 32 * half, tDP = tS + 64;
+    // this warpgroup's 32 columns of a unit: WIDE, all warpgroups share each
+    // unit (columns 32 wg); otherwise pairs alternate units (columns 32 half)
+    const int colw = Cfg::WIDE ? 32 * wg : 32 * half;
+    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + colw, tDP = tS + UK;
+    uint8_t* const sDSw = sDS + (colw / 64) * BWD_BT * 128;
+    const int chunk_half = (colw / 32) & 1;
     const int row = i * BWD_BT + r;
     const int q_abs = row + p.q_offset;
     const int64_t sidx = (int64_t)(b * p.Hq + h) * p.Sq_pad + row;
@@ -812,18 +841,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // kept keys of this row: [q_abs - window + 1, min(q_abs, Skv - 1)]
     const int k_keep_lo = p.window > 0 ? q_abs - p.window + 1 : -0x3fffffff;
     const int k_keep_hi = min(p.causal ? q_abs : 0x3fffffff, p.Skv - 1);
-    for (int u = pair; u < n && ok; u += 2) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[pair], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
+    // unit u: barriers u % 2 with phase (u / 2) % 2, dS tile u % 2
+    for (int u = Cfg::WIDE ? 0 : pair; u < n && ok; u += Cfg::WIDE ? 1 : 2) {
+      const int bb = u & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->sp_full[bb], (u >> 1) & 1, p.ec, abort_flag, SITE_BWD_SP));
       if (!ok) break;
       tc_fence_after();
-      const int c0 = (j_lo + u) * BWD_BS + 32 * half;
+      const int c0 = (j_lo + u) * UK + colw;
       const int keep_lo = k_keep_lo - c0, keep_hi = k_keep_hi - c0;
       const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31);
-      ok = bwd_unit<T, false, false>(p, tS, tDP, &bars->tmem_free[pair], nullptr, nullptr, row_nl2, row_dl,
-                                     keep_lo, keep_hi, masked, &bars->pt_free[pair],
-                                     u >= 2 ? ((u - 2) >> 1) & 1 : -1, abort_flag, nullptr, sDS + pair * Cfg::DS, r,
-                                     half);
-      if (lane == 0) mbar_arrive(&bars->ds_ready[pair]);
+      ok = bwd_unit<T, false, false>(p, tS, tDP, &bars->tmem_free[bb], nullptr, nullptr, row_nl2, row_dl,
+                                     keep_lo, keep_hi, masked, &bars->pt_free[bb],
+                                     u >= 2 ? ((u - 2) >> 1) & 1 : -1, abort_flag, nullptr, sDSw + bb * Cfg::DS, r,
+                                     chunk_half);
+      if (lane == 0) mbar_arrive(&bars->ds_ready[bb]);
     }
     // epilogue: warpgroup w stores dQ columns [w D/4, (w+1) D/4)
     const bool have = ok && n > 0 &&
