@@ -423,8 +423,12 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, u
 // smem.  Whichever is ready goes first, so the tensor core runs one unit's
 // accumulation while the compute warps read the next unit's scores.  The
 // accumulations are issued in unit order, so the sums are deterministic.
+// Streamed operands: one ring of ns_stages slots (st_full / st_empty[0, ns)),
+// released when the unit's accumulation is done; or, with nsv > 0, a second
+// ring (st_full / st_empty[4, 4 + nsv)) that the S / dP MMAs alone read and
+// that is released as soon as they are done (the dQ kernel's V).
 template <int NBUF, typename IssueS, typename IssueAcc>
-__device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_stages, const ErrCtx& ec,
+__device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_stages, int nsv, const ErrCtx& ec,
                                                  volatile int* abort_flag, IssueS issue_s, IssueAcc issue_acc) {
   int ns = 0, na = 0;
   long long t_last = clock64();
@@ -432,10 +436,12 @@ __device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_st
   while (na < n) {
     bool progressed = false;
     if (ns < n && mbar_poll(&bars->st_full[ns % ns_stages], (ns / ns_stages) & 1) &&
+        (nsv == 0 || mbar_poll(&bars->st_full[4 + ns % nsv], (ns / nsv) & 1)) &&
         (ns < NBUF || mbar_poll(&bars->tmem_free[(ns - NBUF) & 1], ((ns - NBUF) >> 1) & 1))) {
       tc_fence_after();
       issue_s(ns);
       mma_commit(&bars->sp_full[ns & 1]);
+      if (nsv) mma_commit(&bars->st_empty[4 + ns % nsv]);
       ++ns;
       progressed = true;
     }
@@ -611,7 +617,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, p.ec, abort_flag, issue_s, issue_acc);
+      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s, issue_acc);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
@@ -720,10 +726,19 @@ struct DqCfg {
   static constexpr int DO_OFF = TILE_Q;
   static constexpr int STAGE_OFF = TILE_Q + TILE_DO + (DS_ALIAS ? 0 : 2 * DS);
   static constexpr int DS_OFF = DS_ALIAS ? 0 : TILE_Q + TILE_DO;  // tile b at b*DS
-  static constexpr int NS = (227 * 1024 - 256 - 1024 - STAGE_OFF) / STAGE > 8 ? 8
-                            : (227 * 1024 - 256 - 1024 - STAGE_OFF) / STAGE;  // stages of {K, V}
-  static_assert(NS >= 2, "dQ smem budget");
-  static constexpr int BAR_OFF = STAGE_OFF + NS * STAGE;
+  static constexpr int BUDGET = 227 * 1024 - 256 - 1024 - STAGE_OFF;
+  // WIDE: K and V in separate rings (V is released when the S / dP MMAs are
+  // done, K when the dQ accumulation is).  Otherwise NS stages of {K, V}.
+  static constexpr bool SPLIT = WIDE && D == DV;
+  static constexpr int SLOTS = BUDGET / SUB_K;
+  static constexpr int NSV = SPLIT ? (SLOTS / 2 < 4 ? SLOTS / 2 : 4) : 0;
+  static constexpr int NSK = SPLIT ? (SLOTS - NSV < 4 ? SLOTS - NSV : 4) : (BUDGET / STAGE > 4 ? 4 : BUDGET / STAGE);
+  static_assert(NSK >= 2 && (!SPLIT || NSV >= 2), "dQ smem budget");
+  __host__ __device__ static constexpr int k_off(int u) { return SPLIT ? (u % NSK) * SUB_K : (u % NSK) * STAGE; }
+  __host__ __device__ static constexpr int v_off(int u) {
+    return SPLIT ? NSK * SUB_K + (u % NSV) * SUB_V : (u % NSK) * STAGE + SUB_K;
+  }
+  static constexpr int BAR_OFF = STAGE_OFF + (SPLIT ? NSK * SUB_K + NSV * SUB_V : NSK * STAGE);
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
@@ -733,7 +748,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                       const BwdParams p) {
   using Cfg = DqCfg<D, DV>;
-  constexpr int NS = Cfg::NS;
+  constexpr int NSK = Cfg::NSK, NSV = Cfg::NSV;
   constexpr int NBUF = Cfg::NBUF;
   constexpr int UK = Cfg::UK;
   constexpr uint32_t TM_ACC = Cfg::TM_AC;
@@ -765,7 +780,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int n = max(0, j_hi - j_lo);
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (threadIdx.x == 0) bwd_init_bars(bars, NS, Cfg::WIDE ? 4 * 4 : 2 * 4);
+  if (threadIdx.x == 0) bwd_init_bars(bars, 8, Cfg::WIDE ? 4 * 4 : 2 * 4);
   if (warp == BWD_WARP_MMA) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -788,27 +803,45 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           tma_load_4d(&tmDO, &bars->fixed_full, sDO + c * BWD_BT * 128 + hf * BWD_BS * 128, c * 64,
                       i * BWD_BT + hf * BWD_BS, h, b, pol_q);
       }
-      int issued = 0;
+      // unit u: V (SPLIT) into its own ring first, since its slot frees first;
+      // then K (or {K, V}) into slot u % NSK
+      int issued_k = 0, issued_v = 0;
       for (int u = 0; u < n; ++u) {
-        const int s = u % NS, use = u / NS;
-        if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
         const int jj = j_lo + u;
-        mbar_arrive_expect_tx(&bars->st_full[s], Cfg::STAGE);
-        uint8_t* dst = sStage + s * Cfg::STAGE;
+        if (Cfg::SPLIT) {
+          const int sv = 4 + u % NSV, usev = u / NSV;
+          if (usev > 0 && !mbar_wait(&bars->st_empty[sv], (usev - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
+          mbar_arrive_expect_tx(&bars->st_full[sv], Cfg::SUB_V);
+          uint8_t* dv = sStage + Cfg::v_off(u);
+          for (int hf = 0; hf < R; ++hf)
+            for (int c = 0; c < DV / 64; ++c)
+              tma_load_4d(&tmV, &bars->st_full[sv], dv + c * UK * 128 + hf * BWD_BS * 128, c * 64,
+                          jj * UK + hf * BWD_BS, hkv, b, pol_kv);
+          ++issued_v;
+        }
+        const int s = u % NSK, use = u / NSK;
+        if (use > 0 && !mbar_wait(&bars->st_empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_BWD_EMPTY)) break;
+        mbar_arrive_expect_tx(&bars->st_full[s], Cfg::SPLIT ? Cfg::SUB_K : Cfg::STAGE);
+        uint8_t* dk = sStage + Cfg::k_off(u);
+        uint8_t* dv = sStage + Cfg::v_off(u);
         for (int hf = 0; hf < R; ++hf) {
           for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(&tmK, &bars->st_full[s], dst + c * UK * 128 + hf * BWD_BS * 128, c * 64,
+            tma_load_4d(&tmK, &bars->st_full[s], dk + c * UK * 128 + hf * BWD_BS * 128, c * 64,
                         jj * UK + hf * BWD_BS, hkv, b, pol_kv);
-          for (int c = 0; c < DV / 64; ++c)
-            tma_load_4d(&tmV, &bars->st_full[s], dst + Cfg::SUB_K + c * UK * 128 + hf * BWD_BS * 128, c * 64,
-                        jj * UK + hf * BWD_BS, hkv, b, pol_kv);
+          if (!Cfg::SPLIT)
+            for (int c = 0; c < DV / 64; ++c)
+              tma_load_4d(&tmV, &bars->st_full[s], dv + c * UK * 128 + hf * BWD_BS * 128, c * 64,
+                          jj * UK + hf * BWD_BS, hkv, b, pol_kv);
         }
-        ++issued;
+        ++issued_k;
       }
       if (*abort_flag) {
         mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
-        for (int u = max(0, issued - NS); u < issued; ++u)
-          mbar_wait(&bars->st_full[u % NS], (u / NS) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+        for (int u = max(0, issued_k - NSK); u < issued_k; ++u)
+          mbar_wait(&bars->st_full[u % NSK], (u / NSK) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+        if (Cfg::SPLIT)
+          for (int u = max(0, issued_v - NSV); u < issued_v; ++u)
+            mbar_wait(&bars->st_full[4 + u % NSV], (u / NSV) & 1, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       }
     }
     __syncwarp();
@@ -822,18 +855,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint32_t tQ = tmem + Cfg::TM_Q, tDO = tmem + Cfg::TM_DO;
       const uint32_t tDQ = tmem + TM_ACC;
       auto issue_s = [&](int u) {
-        const int s = u % NS;
         const uint32_t tS = tmem + Cfg::TM_SC + 2 * UK * (u % NBUF), tDP = tS + UK;
-        const uint64_t k_k = st_kdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
-        const uint64_t v_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_K) >> 4);
+        const uint64_t k_k = st_kdesc + (uint64_t)(Cfg::k_off(u) >> 4);
+        const uint64_t v_k = st_kdesc + (uint64_t)(Cfg::v_off(u) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, UK), idesc_s, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, UK), idesc_s, ks > 0);
       };
       auto issue_acc = [&](int v) {
-        const int bb = v & 1, s = v % NS;
-        const uint64_t k_m = st_mdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
+        const int bb = v & 1;
+        const uint64_t k_m = st_mdesc + (uint64_t)(Cfg::k_off(v) >> 4);
         const uint64_t ds_k = ds_desc + (uint64_t)((bb * Cfg::DS) >> 4);
 #pragma unroll
         for (int ks = 0; ks < UK / 16; ++ks)
@@ -841,7 +873,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, p.ec, abort_flag, issue_s, issue_acc);
+      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, Cfg::NSK, Cfg::NSV, p.ec, abort_flag, issue_s, issue_acc);
       mma_commit(&bars->acc_done);
       if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
     }
