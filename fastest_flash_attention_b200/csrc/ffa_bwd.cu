@@ -485,14 +485,20 @@ struct DkdvCfg {
   static constexpr int SUB_Q = BWD_BS * D * 2;      // Q sub-tile (64 rows)
   static constexpr int SUB_DO = BWD_BS * DV * 2;    // dO sub-tile
   static constexpr int STAGE = SUB_Q + SUB_DO;
-  static constexpr int NS = D == 64 ? 6 : (D == 128 ? 3 : 2);  // stages of {Q, dO, stats}
   static constexpr int PT = BWD_BT * BWD_BS * 2;  // one P^T or dS^T tile (128 x 64, 16-bit)
+  // With K and V both in TMEM their smem is free once copied: the four P^T /
+  // dS^T tiles reuse it, which leaves room for one more {Q, dO} stage.
+  static constexpr bool PT_ALIAS = K_TMEM && 4 * PT <= TILE_K + TILE_V;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_K;
-  static constexpr int STAGE_OFF = TILE_K + TILE_V;        // stage s: Q at s*STAGE, dO at s*STAGE + SUB_Q
-  static constexpr int PT_OFF = STAGE_OFF + NS * STAGE;    // pair b: P^T at b*PT, dS^T at (2+b)*PT
-  static constexpr int STAT_OFF = PT_OFF + 4 * PT;         // stage s: nlse2[64], delta[64]
-  static constexpr int BAR_OFF = STAT_OFF + NS * 2 * BWD_BS * 4;
+  static constexpr int STAGE_OFF = TILE_K + TILE_V + (PT_ALIAS ? 0 : 4 * PT);  // stage s: Q at s*STAGE, dO after
+  static constexpr int PT_OFF = PT_ALIAS ? 0 : TILE_K + TILE_V;  // pair b: P^T at b*PT, dS^T at (2+b)*PT
+  static constexpr int STAT = 2 * BWD_BS * 4;                    // nlse2[64], delta[64]
+  static constexpr int NS_FIT = (227 * 1024 - 256 - 1024 - STAGE_OFF) / (STAGE + STAT);
+  static constexpr int NS = NS_FIT > 8 ? 8 : NS_FIT;  // stages of {Q, dO, stats}
+  static_assert(NS >= 2, "dK/dV smem budget");
+  static constexpr int STAT_OFF = STAGE_OFF + NS * STAGE;  // stage s: stats at s*STAT
+  static constexpr int BAR_OFF = STAT_OFF + NS * STAT;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
