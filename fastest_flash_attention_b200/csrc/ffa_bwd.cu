@@ -28,7 +28,8 @@
 //               D <= 128: every warpgroup serves every 128-key unit, columns
 //               [32 w, 32 w + 32).  One TMEM lane = one row.
 //   warp 16     TMA producer
-//   warp 17     MMA issuer, TMEM owner
+//   warp 17     S / dP MMA issuer, TMEM owner
+//   warp 18     accumulation MMA issuer
 // dK and dQ are multiplied by the softmax scale in their epilogues.
 // TMEM: the kept tile (16-bit A operands), then the score buffers (S or S^T,
 // then dP or dP^T), then the fp32 accumulators; offsets in DkdvCfg / DqCfg.
@@ -40,9 +41,10 @@ namespace ffa {
 constexpr int BWD_BT = 128;       // rows of the tile a CTA keeps (keys in dK/dV, queries in dQ)
 constexpr int BWD_BS = 64;        // rows of a streamed sub-tile
 constexpr int BWD_NWG = 4;         // compute warpgroups: two per TMEM buffer, 32 columns each
-constexpr int BWD_THREADS = BWD_NWG * 128 + 64;  // + TMA warp + MMA warp
+constexpr int BWD_THREADS = BWD_NWG * 128 + 96;  // + TMA warp + two MMA-issuing warps
 constexpr int BWD_WARP_LOAD = BWD_NWG * 4;
-constexpr int BWD_WARP_MMA = BWD_NWG * 4 + 1;
+constexpr int BWD_WARP_MMA = BWD_NWG * 4 + 1;    // S / dP MMAs; TMEM owner
+constexpr int BWD_WARP_ACC = BWD_NWG * 4 + 2;    // accumulation MMAs
 
 struct BwdParams {
   // dK/dV kernel outputs
@@ -369,7 +371,8 @@ struct BwdBars {
   uint64_t tmem_free[2];  // S and dP of unit u read out of TMEM (one arrival per warp of its pair)
   uint64_t ds_ready[2];   // P / dS of unit u stored to smem (one arrival per warp of its pair)
   uint64_t pt_free[2];    // accumulation MMAs of unit u done with its P / dS smem tiles
-  uint64_t acc_done;
+  uint64_t acc_done;      // all accumulation MMAs done
+  uint64_t s_done;        // all S / dP MMAs done
   uint32_t tmem_base;
   int abort;
 };
@@ -393,6 +396,7 @@ __device__ __forceinline__ void bwd_init_bars(BwdBars* bars, int ns, int consume
     mbar_init(&bars->pt_free[t], 1);
   }
   mbar_init(&bars->acc_done, 1);
+  mbar_init(&bars->s_done, 1);
   bars->abort = 0;
   fence_mbar_init();
 }
@@ -417,52 +421,47 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, u
   }
 }
 
-// The MMA issuer's schedule.  S / dP of unit u (into TMEM score buffer
-// u % NBUF) may start once unit u-NBUF's scores are out of TMEM and u's
-// streamed operands have landed; the accumulation MMAs of unit u once its P / dS are in
-// smem.  Whichever is ready goes first, so the tensor core runs one unit's
-// accumulation while the compute warps read the next unit's scores.  The
-// accumulations are issued in unit order, so the sums are deterministic.
+// The MMAs are issued by two threads in different warps, so that one never
+// waits behind the other's issue (an issuing thread stalls while the tensor
+// core's queue is full):
+//  * bwd_issue_scores: S / dP of unit u (into TMEM score buffer u % NBUF) once
+//    u's streamed operands have landed and unit u-NBUF's scores are out of TMEM;
+//  * bwd_issue_acc: the accumulation MMAs of unit u once its P / dS are in
+//    smem, in unit order, so the sums are deterministic.
 // Streamed operands: one ring of ns_stages slots (st_full / st_empty[0, ns)),
 // released when the unit's accumulation is done; or, with nsv > 0, a second
 // ring (st_full / st_empty[4, 4 + nsv)) that the S / dP MMAs alone read and
-// that is released as soon as they are done (the dQ kernel's V).
-template <int NBUF, typename IssueS, typename IssueAcc>
-__device__ __forceinline__ bool bwd_mma_schedule(BwdBars* bars, int n, int ns_stages, int nsv, const ErrCtx& ec,
-                                                 volatile int* abort_flag, IssueS issue_s, IssueAcc issue_acc) {
-  int ns = 0, na = 0;
-  long long t_last = clock64();
-  const long long limit = (long long)(ec.limit_ns * 2ull);
-  while (na < n) {
-    bool progressed = false;
-    if (ns < n && mbar_poll(&bars->st_full[ns % ns_stages], (ns / ns_stages) & 1) &&
-        (nsv == 0 || mbar_poll(&bars->st_full[4 + ns % nsv], (ns / nsv) & 1)) &&
-        (ns < NBUF || mbar_poll(&bars->tmem_free[(ns - NBUF) & 1], ((ns - NBUF) >> 1) & 1))) {
-      tc_fence_after();
-      issue_s(ns);
-      mma_commit(&bars->sp_full[ns & 1]);
-      if (nsv) mma_commit(&bars->st_empty[4 + ns % nsv]);
-      ++ns;
-      progressed = true;
-    }
-    if (na < ns && mbar_poll(&bars->ds_ready[na & 1], (na >> 1) & 1)) {
-      tc_fence_after();
-      issue_acc(na);
-      mma_commit(&bars->st_empty[na % ns_stages]);
-      mma_commit(&bars->pt_free[na & 1]);
-      ++na;
-      progressed = true;
-    }
-    if (progressed) {
-      t_last = clock64();
-    } else {
-      if (*abort_flag) return false;
-      if (clock64() - t_last > limit) {
-        *abort_flag = 1;
-        if (ec.err) atomicCAS(ec.err, 0u, (uint32_t)SITE_BWD_DS);
-        return false;
-      }
-    }
+// that is released as soon as they are done (the dQ kernel's V).  A unit's
+// accumulation starts after its S / dP MMAs completed (its P / dS derive from
+// them), so the first ring's slot is free once the accumulation is done.
+template <int NBUF, typename IssueS>
+__device__ __forceinline__ bool bwd_issue_scores(BwdBars* bars, int n, int ns_stages, int nsv, const ErrCtx& ec,
+                                                 volatile int* abort_flag, IssueS issue_s) {
+  for (int u = 0; u < n; ++u) {
+    if (!mbar_wait_mma(&bars->st_full[u % ns_stages], (u / ns_stages) & 1, ec, abort_flag, SITE_BWD_LOAD))
+      return false;
+    if (nsv && !mbar_wait_mma(&bars->st_full[4 + u % nsv], (u / nsv) & 1, ec, abort_flag, SITE_BWD_LOAD))
+      return false;
+    if (u >= NBUF &&
+        !mbar_wait_mma(&bars->tmem_free[(u - NBUF) & 1], ((u - NBUF) >> 1) & 1, ec, abort_flag, SITE_BWD_DS))
+      return false;
+    tc_fence_after();
+    issue_s(u);
+    mma_commit(&bars->sp_full[u & 1]);
+    if (nsv) mma_commit(&bars->st_empty[4 + u % nsv]);
+  }
+  return true;
+}
+
+template <typename IssueAcc>
+__device__ __forceinline__ bool bwd_issue_acc(BwdBars* bars, int n, int ns_stages, const ErrCtx& ec,
+                                              volatile int* abort_flag, IssueAcc issue_acc) {
+  for (int u = 0; u < n; ++u) {
+    if (!mbar_wait_mma(&bars->ds_ready[u & 1], (u >> 1) & 1, ec, abort_flag, SITE_BWD_DS)) return false;
+    tc_fence_after();
+    issue_acc(u);
+    mma_commit(&bars->st_empty[u % ns_stages]);
+    mma_commit(&bars->pt_free[u & 1]);
   }
   return true;
 }
@@ -581,7 +580,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == BWD_WARP_MMA) {
+  } else if (warp == BWD_WARP_MMA || warp == BWD_WARP_ACC) {
     if (lane == 0 && n > 0) {
       const uint32_t idesc_t = make_idesc_f16(128, BWD_BS, FMT, 0, 0);  // S^T, dP^T (K-major A x K-major B)
       const uint32_t idesc_dv = make_idesc_f16(128, DV, FMT, 0, 1);     // dV (K-major A x MN-major B)
@@ -622,10 +621,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           mma_ss(tDK, ds_k + kstep(ks, BWD_BT), q_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dk,
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s, issue_acc);
-      mma_commit(&bars->acc_done);
-      if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      if (warp == BWD_WARP_MMA) {
+        bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s);
+        mma_commit(&bars->s_done);
+        if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      } else {
+        const bool ok = bwd_issue_acc(bars, n, NS, p.ec, abort_flag, issue_acc);
+        mma_commit(&bars->acc_done);
+        if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      }
     }
     __syncwarp();
   } else {
@@ -851,7 +856,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == BWD_WARP_MMA) {
+  } else if (warp == BWD_WARP_MMA || warp == BWD_WARP_ACC) {
     if (lane == 0 && n > 0) {
       const uint32_t idesc_s = make_idesc_f16(128, UK, FMT, 0, 0);  // S, dP (TMEM A x K-major B)
       const uint32_t idesc_dq = make_idesc_f16(128, D, FMT, 0, 1);  // dQ (K-major A x MN-major B)
@@ -878,10 +883,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           mma_ss(tDQ, ds_k + kstep(ks, BWD_BT), k_m + (uint64_t)((ks * 16 * 128) >> 4), idesc_dq,
                  (v > 0 || ks > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-      if (ok) ok = bwd_mma_schedule<NBUF>(bars, n, Cfg::NSK, Cfg::NSV, p.ec, abort_flag, issue_s, issue_acc);
-      mma_commit(&bars->acc_done);
-      if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      if (warp == BWD_WARP_MMA) {
+        bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NSK, NSV, p.ec, abort_flag, issue_s);
+        mma_commit(&bars->s_done);
+        if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      } else {
+        const bool ok = bwd_issue_acc(bars, n, NSK, p.ec, abort_flag, issue_acc);
+        mma_commit(&bars->acc_done);
+        if (!ok) mbar_wait(&bars->acc_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
+      }
     }
     __syncwarp();
   } else {

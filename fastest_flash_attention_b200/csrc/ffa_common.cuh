@@ -119,6 +119,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// The MMA issuer's wait: a non-blocking probe first (cheap when the phase is
+// already complete, the common case), then the bounded blocking wait.
+__device__ __forceinline__ bool mbar_wait_mma(uint64_t* bar, uint32_t parity, const ErrCtx& ec, volatile int* abort,
+                                              uint32_t site, bool drain = false) {
+  if (mbar_poll(bar, parity)) return true;
+  return mbar_wait(bar, parity, ec, abort, site, drain);
+}
+
 // ---------------------------------- TMA ------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");

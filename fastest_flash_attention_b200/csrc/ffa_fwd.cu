@@ -23,13 +23,6 @@
 #include "ffa_host.h"
 
 namespace ffa {
-// The MMA issuer's wait: a non-blocking probe first (cheap when the phase is
-// already complete, the common case), then the bounded blocking wait.
-__device__ __forceinline__ bool mbar_wait_mma(uint64_t* bar, uint32_t parity, const ErrCtx& ec, volatile int* abort,
-                                              uint32_t site, bool drain = false) {
-  if (mbar_poll(bar, parity)) return true;
-  return mbar_wait(bar, parity, ec, abort, site, drain);
-}
 
 constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
 constexpr int FWD_NQT = 2;    // query tiles per CTA
