@@ -189,6 +189,8 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, uint
 // P / dS for this thread's 32 columns of a unit (one TMEM row = tile row
 // `row`).  tS / tDP address the first of the 32 columns; the TMEM buffer is
 // released (arrive on `tmem_free`) as soon as the values are in registers.
+// (Releasing S before dP is read was measured slower: the two loads then
+// no longer overlap.)
 // Column statistics come from smem (COL_STATS: cnl2 / cdl for the first
 // column) or are the row's (rnl2, rdl).  The row keeps columns
 // [keep_lo, keep_hi] of the 32; `masked` (warp-uniform) is false when no row
@@ -368,7 +370,7 @@ struct BwdBars {
   uint64_t st_full[8];
   uint64_t st_empty[8];
   uint64_t sp_full[2];    // S and dP of unit u computed (index u % 2)
-  uint64_t tmem_free[2];  // S and dP of unit u read out of TMEM (one arrival per warp of its pair)
+  uint64_t tmem_free[2];  // S and dP of unit u read out of TMEM (one arrival per consuming warp)
   uint64_t ds_ready[2];   // P / dS of unit u stored to smem (one arrival per warp of its pair)
   uint64_t pt_free[2];    // accumulation MMAs of unit u done with its P / dS smem tiles
   uint64_t acc_done;      // all accumulation MMAs done
@@ -434,9 +436,9 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, u
 // that is released as soon as they are done (the dQ kernel's V).  A unit's
 // accumulation starts after its S / dP MMAs completed (its P / dS derive from
 // them), so the first ring's slot is free once the accumulation is done.
-template <int NBUF, typename IssueS>
+template <int NBUF, typename IssueS, typename IssueDP>
 __device__ __forceinline__ bool bwd_issue_scores(BwdBars* bars, int n, int ns_stages, int nsv, const ErrCtx& ec,
-                                                 volatile int* abort_flag, IssueS issue_s) {
+                                                 volatile int* abort_flag, IssueS issue_s, IssueDP issue_dp) {
   for (int u = 0; u < n; ++u) {
     if (!mbar_wait_mma(&bars->st_full[u % ns_stages], (u / ns_stages) & 1, ec, abort_flag, SITE_BWD_LOAD))
       return false;
@@ -447,6 +449,7 @@ __device__ __forceinline__ bool bwd_issue_scores(BwdBars* bars, int n, int ns_st
       return false;
     tc_fence_after();
     issue_s(u);
+    issue_dp(u);
     mma_commit(&bars->sp_full[u & 1]);
     if (nsv) mma_commit(&bars->st_empty[4 + u % nsv]);
   }
@@ -469,16 +472,27 @@ __device__ __forceinline__ bool bwd_issue_acc(BwdBars* bars, int n, int ns_stage
 // ---------------------------------------------------------------------------
 // 2. dK / dV
 // ---------------------------------------------------------------------------
-// D = query/key head dim, DV = value head dim.  (D, DV) = (192, 128) is the
-// MLA training shape: its accumulators (dV 128 + dK 192 columns) leave TMEM
-// room for V only, so S^T = K Q^T reads K from smem there.
+// D = query/key head dim, DV = value head dim.  TMEM holds the score
+// buffers (S^T 64 + dP^T 64 columns each), the accumulators (dV, dK) and,
+// as 16-bit A operands of the S^T / dP^T MMAs, V and (when the columns allow)
+// K; otherwise S^T = K Q^T reads K from smem:
+//   D = 64:  K 32 + V 32 + two score buffers + dV 64 + dK 64 columns (two
+//            buffers let unit u+1's S / dP MMAs run while unit u's scores are
+//            still being read out);
+//   D = 128: K 64 + V 64 + one buffer + dV 128 + dK 128;
+//   D = 192 (the MLA training shape): V 64 + one buffer + dV 128 + dK 192.
+// (At D = 128 a second buffer would push K and V to smem and cost a {Q, dO}
+// stage, which measured slower.)
 template <int D, int DV>
 struct DkdvCfg {
+  static constexpr int NBUF = D == 64 ? 2 : 1;
   static constexpr bool K_TMEM = D + DV <= 256;     // K kept in TMEM as an A operand
+  static constexpr bool V_TMEM = true;              // V kept in TMEM as an A operand
   static constexpr uint32_t TM_K = 0;
   static constexpr uint32_t TM_V = K_TMEM ? 64 : 0;
-  static constexpr uint32_t TM_SC = K_TMEM ? 128 : 64;  // the score buffer (S^T 64 + dP^T 64 columns)
-  static constexpr uint32_t TM_AC = TM_SC + 128;       // dV (DV columns) then dK (D columns)
+  static constexpr uint32_t TM_SC = K_TMEM ? 128 : 64;  // score buffer b at TM_SC + 128 b
+  static constexpr uint32_t TM_AC = TM_SC + 128 * NBUF;                // dV (DV columns) then dK (D columns)
+  static_assert(TM_AC + DV + D <= 512, "dK/dV TMEM budget");
   static constexpr int TILE_K = BWD_BT * D * 2;     // K tile (128 rows)
   static constexpr int TILE_V = BWD_BT * DV * 2;    // V tile
   static constexpr int SUB_Q = BWD_BS * D * 2;      // Q sub-tile (64 rows)
@@ -487,7 +501,7 @@ struct DkdvCfg {
   static constexpr int PT = BWD_BT * BWD_BS * 2;  // one P^T or dS^T tile (128 x 64, 16-bit)
   // With K and V both in TMEM their smem is free once copied: the four P^T /
   // dS^T tiles reuse it, which leaves room for one more {Q, dO} stage.
-  static constexpr bool PT_ALIAS = K_TMEM && 4 * PT <= TILE_K + TILE_V;
+  static constexpr bool PT_ALIAS = K_TMEM && V_TMEM && 4 * PT <= TILE_K + TILE_V;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_K;
   static constexpr int STAGE_OFF = TILE_K + TILE_V + (PT_ALIAS ? 0 : 4 * PT);  // stage s: Q at s*STAGE, dO after
@@ -508,7 +522,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                         const BwdParams p) {
   using Cfg = DkdvCfg<D, DV>;
   constexpr int NS = Cfg::NS;
-  constexpr int NBUF = 1;
+  constexpr int NBUF = Cfg::NBUF;
   constexpr uint32_t TM_ACC = Cfg::TM_AC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -589,13 +603,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint64_t st_mdesc = make_sdesc_sw128(smem_u32(sStage), BWD_BS * 128, 1024);
       const uint64_t pt_desc = make_sdesc_sw128(smem_u32(sPT), 16, 1024);
       const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t v_desc = make_sdesc_sw128(smem_u32(sV), 16, 1024);
       const uint32_t tK = tmem + Cfg::TM_K, tV = tmem + Cfg::TM_V;
-      const uint32_t tS = tmem + Cfg::TM_SC, tDP = tmem + Cfg::TM_SC + 64;
       const uint32_t tDV = tmem + TM_ACC, tDK = tmem + TM_ACC + DV;
       auto issue_s = [&](int u) {
         const int s = u % NS;
+        const uint32_t tS = tmem + Cfg::TM_SC + 128 * (u % NBUF);
         const uint64_t q_k = st_kdesc + (uint64_t)((s * Cfg::STAGE) >> 4);
-        const uint64_t do_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_Q) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           if constexpr (Cfg::K_TMEM)
@@ -603,8 +617,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           else
             mma_ss(tS, k_desc + kstep(ks, BWD_BT), q_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
         }
+      };
+      auto issue_dp = [&](int u) {
+        const int s = u % NS;
+        const uint32_t tDP = tmem + Cfg::TM_SC + 128 * (u % NBUF) + 64;
+        const uint64_t do_k = st_kdesc + (uint64_t)((s * Cfg::STAGE + Cfg::SUB_Q) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tV + 8 * ks, do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        for (int ks = 0; ks < DV / 16; ++ks) {
+          if constexpr (Cfg::V_TMEM)
+            mma_ts(tDP, tV + 8 * ks, do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+          else
+            mma_ss(tDP, v_desc + kstep(ks, BWD_BT), do_k + kstep(ks, BWD_BS), idesc_t, ks > 0);
+        }
       };
       auto issue_acc = [&](int v) {
         const int bb = v & 1, s = v % NS;
@@ -623,7 +647,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       };
       if (warp == BWD_WARP_MMA) {
         bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s, issue_dp);
         mma_commit(&bars->s_done);
         if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       } else {
@@ -638,15 +662,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int wg = warp / 4, pair = wg % 2, half = wg / 2;
     const int r = threadIdx.x % 128;  // key row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + 32 * half, tDP = tS + 64;
+    // units alternate between the pairs, and (NBUF = 2) between the buffers
+    const uint32_t tS = tmem + lane_off + Cfg::TM_SC + 128 * (pair % NBUF) + 32 * half, tDP = tS + 64;
     const int key = j * BWD_BT + r;
     bool ok = true;
     if (n > 0 && wg < 2) {  // K (warpgroup 0) / V (warpgroup 1) into TMEM as the A operand
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->fixed_full, 0, p.ec, abort_flag, SITE_BWD_LOAD));
       if (ok) {
-        if (wg == 1)
+        if (wg == 1 && Cfg::V_TMEM)
           tile_row_to_tmem<DV>(sV, r, tmem + lane_off + Cfg::TM_V);
-        else if (Cfg::K_TMEM)
+        else if (wg == 0 && Cfg::K_TMEM)
           tile_row_to_tmem<D>(sK, r, tmem + lane_off + Cfg::TM_K);
         tmem_st_wait();
         tc_fence_before();
@@ -866,11 +891,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint32_t tQ = tmem + Cfg::TM_Q, tDO = tmem + Cfg::TM_DO;
       const uint32_t tDQ = tmem + TM_ACC;
       auto issue_s = [&](int u) {
-        const uint32_t tS = tmem + Cfg::TM_SC + 2 * UK * (u % NBUF), tDP = tS + UK;
+        const uint32_t tS = tmem + Cfg::TM_SC + 2 * UK * (u % NBUF);
         const uint64_t k_k = st_kdesc + (uint64_t)(Cfg::k_off(u) >> 4);
-        const uint64_t v_k = st_kdesc + (uint64_t)(Cfg::v_off(u) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) mma_ts(tS, tQ + 8 * ks, k_k + kstep(ks, UK), idesc_s, ks > 0);
+      };
+      auto issue_dp = [&](int u) {
+        const uint32_t tDP = tmem + Cfg::TM_SC + 2 * UK * (u % NBUF) + UK;
+        const uint64_t v_k = st_kdesc + (uint64_t)(Cfg::v_off(u) >> 4);
 #pragma unroll
         for (int ks = 0; ks < DV / 16; ++ks) mma_ts(tDP, tDO + 8 * ks, v_k + kstep(ks, UK), idesc_s, ks > 0);
       };
@@ -885,7 +913,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       };
       if (warp == BWD_WARP_MMA) {
         bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NSK, NSV, p.ec, abort_flag, issue_s);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NSK, NSV, p.ec, abort_flag, issue_s, issue_dp);
         mma_commit(&bars->s_done);
         if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       } else {
