@@ -112,48 +112,54 @@ __device__ __forceinline__ void k_range_for_q_tile(const BwdParams& p, int i, in
 // (COL_STATS, dK/dV kernel: cnl2 / cdl, 16-byte aligned) or are the row's
 // (rnl2 / rdl, dQ kernel).  With MASKED, columns c with (uint)(c - lo) >= cnt
 // are dropped.  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
-// pipe); 2: softcap with tanh through ex2 / rcp.
+// pipe); 2: softcap with tanh through ex2 / rcp.  Columns are processed in
+// pairs with packed fp32x2 instructions (per lane the same IEEE operations as
+// the scalar forms: dp - dl is computed as dp + dl * -1, and
+// (dp - dl)(1 - th^2) as (dl - dp)(th^2 - 1), both exact rewrites).
 template <typename T, bool WRITE_P, bool COL_STATS, int MODE, bool MASKED>
 __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
                                             const float* cnl2, const float* cdl, float rnl2, float rdl, int lo,
                                             uint32_t cnt, uint32_t* pk_p, uint32_t* pk_ds) {
 #pragma unroll
   for (int c4 = 0; c4 < 16; c4 += 4) {
-    float nl2[4], dl[4];
+    float2 nl2[2], dl[2];
     if (COL_STATS) {
       const float4 a = *reinterpret_cast<const float4*>(cnl2 + c4);
       const float4 z = *reinterpret_cast<const float4*>(cdl + c4);
-      nl2[0] = a.x; nl2[1] = a.y; nl2[2] = a.z; nl2[3] = a.w;
-      dl[0] = z.x; dl[1] = z.y; dl[2] = z.z; dl[3] = z.w;
+      nl2[0] = make_float2(a.x, a.y);
+      nl2[1] = make_float2(a.z, a.w);
+      dl[0] = make_float2(z.x, z.y);
+      dl[1] = make_float2(z.z, z.w);
     } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        nl2[e] = rnl2;
-        dl[e] = rdl;
-      }
+      nl2[0] = nl2[1] = f2(rnl2);
+      dl[0] = dl[1] = f2(rdl);
     }
 #pragma unroll
-    for (int c2 = 0; c2 < 4; c2 += 2) {
-      float pv[2], dv[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = c4 + c2 + u;
-        const float raw = __uint_as_float(s[c]);
-        float pr, g;
-        if (MODE == 0) {
-          pr = ex2(fmaf(raw, p.scale_log2, nl2[c2 + u]));
-          g = __uint_as_float(dp[c]) - dl[c2 + u];
-        } else {
-          const float th = MODE == 1 ? tanh_small(raw * p.sc_pre) : tanh_acc(raw * p.sc_pre);
-          pr = ex2(fmaf(th, p.sc_post, nl2[c2 + u]));
-          g = (__uint_as_float(dp[c]) - dl[c2 + u]) * fmaf(-th, th, 1.f);
-        }
-        if (MASKED) pr = ((uint32_t)(c - lo) < cnt) ? pr : 0.f;
-        pv[u] = pr;
-        dv[u] = pr * g;
+    for (int h = 0; h < 2; ++h) {
+      const int c = c4 + 2 * h;
+      const float2 raw = make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+      const float2 dpv = make_float2(__uint_as_float(dp[c]), __uint_as_float(dp[c + 1]));
+      float2 x, g;
+      if (MODE == 0) {
+        x = ffma2(raw, f2(p.scale_log2), nl2[h]);
+        g = ffma2(dl[h], f2(-1.f), dpv);
+      } else if (MODE == 1) {
+        const float2 th = tanh_small2(fmul2(raw, f2(p.sc_pre)));
+        x = ffma2(th, f2(p.sc_post), nl2[h]);
+        g = fmul2(ffma2(dpv, f2(-1.f), dl[h]), ffma2(th, th, f2(-1.f)));
+      } else {
+        const float t0 = tanh_acc(raw.x * p.sc_pre), t1 = tanh_acc(raw.y * p.sc_pre);
+        x = make_float2(fmaf(t0, p.sc_post, nl2[h].x), fmaf(t1, p.sc_post, nl2[h].y));
+        g = make_float2((dpv.x - dl[h].x) * fmaf(-t0, t0, 1.f), (dpv.y - dl[h].y) * fmaf(-t1, t1, 1.f));
       }
-      if (WRITE_P) pk_p[(c4 + c2) / 2] = pack2<T>(pv[0], pv[1]);
-      pk_ds[(c4 + c2) / 2] = pack2<T>(dv[0], dv[1]);
+      float2 pr = make_float2(ex2(x.x), ex2(x.y));
+      if (MASKED) {
+        pr.x = ((uint32_t)(c - lo) < cnt) ? pr.x : 0.f;
+        pr.y = ((uint32_t)(c + 1 - lo) < cnt) ? pr.y : 0.f;
+      }
+      const float2 dv = fmul2(pr, g);
+      if (WRITE_P) pk_p[c / 2] = pack2<T>(pr.x, pr.y);
+      pk_ds[c / 2] = pack2<T>(dv.x, dv.y);
     }
   }
 }
@@ -427,7 +433,9 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, u
 // waits behind the other's issue (an issuing thread stalls while the tensor
 // core's queue is full):
 //  * bwd_issue_scores: S / dP of unit u (into TMEM score buffer u % NBUF) once
-//    u's streamed operands have landed and unit u-NBUF's scores are out of TMEM;
+//    u's streamed operands have landed and unit u-NBUF is done with the
+//    buffer (`buf_free`: its scores read out, or, when P / dS are kept in the
+//    buffer, its accumulation MMAs done);
 //  * bwd_issue_acc: the accumulation MMAs of unit u once its P / dS are in
 //    smem, in unit order, so the sums are deterministic.
 // Streamed operands: one ring of ns_stages slots (st_full / st_empty[0, ns)),
@@ -437,15 +445,15 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int row, u
 // accumulation starts after its S / dP MMAs completed (its P / dS derive from
 // them), so the first ring's slot is free once the accumulation is done.
 template <int NBUF, typename IssueS, typename IssueDP>
-__device__ __forceinline__ bool bwd_issue_scores(BwdBars* bars, int n, int ns_stages, int nsv, const ErrCtx& ec,
-                                                 volatile int* abort_flag, IssueS issue_s, IssueDP issue_dp) {
+__device__ __forceinline__ bool bwd_issue_scores(BwdBars* bars, uint64_t* buf_free, int n, int ns_stages, int nsv,
+                                                 const ErrCtx& ec, volatile int* abort_flag, IssueS issue_s,
+                                                 IssueDP issue_dp) {
   for (int u = 0; u < n; ++u) {
     if (!mbar_wait_mma(&bars->st_full[u % ns_stages], (u / ns_stages) & 1, ec, abort_flag, SITE_BWD_LOAD))
       return false;
     if (nsv && !mbar_wait_mma(&bars->st_full[4 + u % nsv], (u / nsv) & 1, ec, abort_flag, SITE_BWD_LOAD))
       return false;
-    if (u >= NBUF &&
-        !mbar_wait_mma(&bars->tmem_free[(u - NBUF) & 1], ((u - NBUF) >> 1) & 1, ec, abort_flag, SITE_BWD_DS))
+    if (u >= NBUF && !mbar_wait_mma(&buf_free[(u - NBUF) & 1], ((u - NBUF) >> 1) & 1, ec, abort_flag, SITE_BWD_DS))
       return false;
     tc_fence_after();
     issue_s(u);
@@ -474,24 +482,28 @@ __device__ __forceinline__ bool bwd_issue_acc(BwdBars* bars, int n, int ns_stage
 // ---------------------------------------------------------------------------
 // D = query/key head dim, DV = value head dim.  TMEM holds the score
 // buffers (S^T 64 + dP^T 64 columns each), the accumulators (dV, dK) and,
-// as 16-bit A operands of the S^T / dP^T MMAs, V and (when the columns allow)
-// K; otherwise S^T = K Q^T reads K from smem:
-//   D = 64:  K 32 + V 32 + two score buffers + dV 64 + dK 64 columns (two
+// where the columns allow, K and V as 16-bit A operands (else the S^T / dP^T
+// MMAs read them from smem):
+//   D = 64:  K + V (64 columns each) + two score buffers + dV 64 + dK 64; two
 //            buffers let unit u+1's S / dP MMAs run while unit u's scores are
-//            still being read out);
-//   D = 128: K 64 + V 64 + one buffer + dV 128 + dK 128;
-//   D = 192 (the MLA training shape): V 64 + one buffer + dV 128 + dK 192.
-// (At D = 128 a second buffer would push K and V to smem and cost a {Q, dO}
-// stage, which measured slower.)
+//            still being read out;
+//   D = 128: K + V + one buffer + dV 128 + dK 128 (a second buffer would push
+//            K and V to smem and cost a {Q, dO} stage: measured slower);
+//   D = 192 (the MLA training shape): V + one buffer + dV 128 + dK 192.
+// P^T / dS^T go through smem.  (Writing them back over their TMEM score
+// columns, so the accumulation MMAs read them from TMEM, with two buffers at
+// D = 128, measured no faster.)
 template <int D, int DV>
 struct DkdvCfg {
   static constexpr int NBUF = D == 64 ? 2 : 1;
-  static constexpr bool K_TMEM = D + DV <= 256;     // K kept in TMEM as an A operand
-  static constexpr bool V_TMEM = true;              // V kept in TMEM as an A operand
+  // TMEM columns left for K / V (64 each) after the score buffers and dV, dK
+  static constexpr int KV_COLS = 512 - 128 * NBUF - (D + DV);
+  static constexpr bool V_TMEM = KV_COLS >= 64;   // V kept in TMEM as an A operand
+  static constexpr bool K_TMEM = KV_COLS >= 128;  // K kept in TMEM as an A operand
   static constexpr uint32_t TM_K = 0;
   static constexpr uint32_t TM_V = K_TMEM ? 64 : 0;
-  static constexpr uint32_t TM_SC = K_TMEM ? 128 : 64;  // score buffer b at TM_SC + 128 b
-  static constexpr uint32_t TM_AC = TM_SC + 128 * NBUF;                // dV (DV columns) then dK (D columns)
+  static constexpr uint32_t TM_SC = (K_TMEM ? 64 : 0) + (V_TMEM ? 64 : 0);  // buffer b at TM_SC + 128 b
+  static constexpr uint32_t TM_AC = TM_SC + 128 * NBUF;  // dV (DV columns) then dK (D columns)
   static_assert(TM_AC + DV + D <= 512, "dK/dV TMEM budget");
   static constexpr int TILE_K = BWD_BT * D * 2;     // K tile (128 rows)
   static constexpr int TILE_V = BWD_BT * DV * 2;    // V tile
@@ -501,10 +513,11 @@ struct DkdvCfg {
   static constexpr int PT = BWD_BT * BWD_BS * 2;  // one P^T or dS^T tile (128 x 64, 16-bit)
   // With K and V both in TMEM their smem is free once copied: the four P^T /
   // dS^T tiles reuse it, which leaves room for one more {Q, dO} stage.
+  // smem P^T / dS^T tiles reuse the K / V smem when both are in TMEM by then
   static constexpr bool PT_ALIAS = K_TMEM && V_TMEM && 4 * PT <= TILE_K + TILE_V;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_K;
-  static constexpr int STAGE_OFF = TILE_K + TILE_V + (PT_ALIAS ? 0 : 4 * PT);  // stage s: Q at s*STAGE, dO after
+  static constexpr int STAGE_OFF = TILE_K + TILE_V + (PT_ALIAS ? 0 : 4 * PT);  // Q at s*STAGE, dO after
   static constexpr int PT_OFF = PT_ALIAS ? 0 : TILE_K + TILE_V;  // pair b: P^T at b*PT, dS^T at (2+b)*PT
   static constexpr int STAT = 2 * BWD_BS * 4;                    // nlse2[64], delta[64]
   static constexpr int NS_FIT = (227 * 1024 - 256 - 1024 - STAGE_OFF) / (STAGE + STAT);
@@ -647,7 +660,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       };
       if (warp == BWD_WARP_MMA) {
         bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NS, 0, p.ec, abort_flag, issue_s, issue_dp);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, bars->tmem_free, n, NS, 0, p.ec, abort_flag, issue_s, issue_dp);
         mma_commit(&bars->s_done);
         if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       } else {
@@ -913,7 +926,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       };
       if (warp == BWD_WARP_MMA) {
         bool ok = mbar_wait(&bars->fixed_tmem, 0, p.ec, abort_flag, SITE_BWD_LOAD);
-        if (ok) ok = bwd_issue_scores<NBUF>(bars, n, NSK, NSV, p.ec, abort_flag, issue_s, issue_dp);
+        if (ok) ok = bwd_issue_scores<NBUF>(bars, bars->tmem_free, n, NSK, NSV, p.ec, abort_flag, issue_s, issue_dp);
         mma_commit(&bars->s_done);
         if (!ok) mbar_wait(&bars->s_done, 0, p.ec, abort_flag, SITE_BWD_DRAIN, true);
       } else {

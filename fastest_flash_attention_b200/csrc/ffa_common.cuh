@@ -348,6 +348,28 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return d;
 }
 
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+// tanh_small for two lanes with packed instructions; the same operations in
+// the same order per lane, so the results are bit-identical to tanh_small.
+__device__ __forceinline__ float2 tanh_small2(float2 x) {
+  const float2 x2 = fmul2(x, x);
+  float2 p = ffma2(f2(-8.8632e-3f), x2, f2(2.1869488536155203e-2f));
+  p = ffma2(p, x2, f2(-5.3968253968253971e-2f));
+  p = ffma2(p, x2, f2(1.3333333333333333e-1f));
+  p = ffma2(p, x2, f2(-3.3333333333333333e-1f));
+  return ffma2(fmul2(p, x2), x, x);
+}
+
 // 2^x on the FMA pipe, for two lanes at once, to offload the MUFU unit.
 // x = n + f with n = rint(x) (magic-constant rounding), f in [-1/2, 1/2];
 // 2^f by a cubic whose coefficients are the relative-error minimax fit from
