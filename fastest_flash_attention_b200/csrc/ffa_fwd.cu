@@ -362,9 +362,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         for (int c = 0; c < FWD_BN; c += 2)
           amax = fmax3(amax, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
         if (__all_sync(0xffffffffu, amax * fabsf(p.sc_pre) <= 0.5f)) {
+          // pairs with packed instructions (per lane the same operations)
 #pragma unroll
-          for (int c = 0; c < FWD_BN; ++c)
-            s[c] = __float_as_uint(tanh_small(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+          for (int c = 0; c < FWD_BN; c += 2) {
+            const float2 th = tanh_small2(
+                fmul2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), f2(p.sc_pre)));
+            const float2 v = fmul2(th, f2(p.sc_post));
+            s[c] = __float_as_uint(v.x);
+            s[c + 1] = __float_as_uint(v.y);
+          }
         } else {
 #pragma unroll
           for (int c = 0; c < FWD_BN; ++c)
