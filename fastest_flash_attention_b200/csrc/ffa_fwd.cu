@@ -450,7 +450,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           tmem_ld32(tO + c, ov);
           tmem_ld_wait32(ov);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          for (int e = 0; e < 32; e += 2) {
+            const float2 v = fmul2(make_float2(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), f2(alpha));
+            ov[e] = __float_as_uint(v.x);
+            ov[e + 1] = __float_as_uint(v.y);
+          }
           tmem_st32(tO + c, ov);
         }
       }
@@ -509,8 +513,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       }
       uint32_t pk[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        pk[e] = pack2<T>(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
+      for (int e = 0; e < 16; ++e) {
+        const float2 v = fmul2(make_float2(__uint_as_float(ov[2 * e]), __uint_as_float(ov[2 * e + 1])), f2(inv_l));
+        pk[e] = pack2<T>(v.x, v.y);
+      }
       if (store) {
         uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
