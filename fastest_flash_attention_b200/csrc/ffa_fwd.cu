@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < FWD_BN; c += 32) tmem_ld_wait32(s + c);
       // Scores in base-2 units are  s * mul  (mul = scale*log2 e), or, with a
-      // softcap, softcap*tanh(s*scale/softcap)*log2 e computed in place (mul = 1).
+      // softcap, tanh(s*scale/softcap) computed in place (mul = softcap*log2 e).
       float mul = p.scale_log2;
       if (p.use_softcap) {
         // tanh(s*scale/softcap): the FMA-pipe series when every argument of
@@ -367,16 +367,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           for (int c = 0; c < FWD_BN; c += 2) {
             const float2 th = tanh_small2(
                 fmul2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), f2(p.sc_pre)));
-            const float2 v = fmul2(th, f2(p.sc_post));
-            s[c] = __float_as_uint(v.x);
-            s[c + 1] = __float_as_uint(v.y);
+            s[c] = __float_as_uint(th.x);
+            s[c + 1] = __float_as_uint(th.y);
           }
         } else {
 #pragma unroll
           for (int c = 0; c < FWD_BN; ++c)
-            s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre) * p.sc_post);
+            s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre));
         }
-        mul = 1.f;
+        mul = p.sc_post;  // softcap*log2(e) > 0: applied in the exponent's FMA
       }
       const int c0 = j * FWD_BN;
       const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) ||
