@@ -1010,18 +1010,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
-template <typename K>
-static int set_smem(K kern, int bytes) {
-  return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-}
-
 template <typename T, int D, int DV>
 static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o, const void* dout,
                       const float* lse, float* lse2, float* delta, const int64_t* o_str, const int64_t* do_str,
                       cudaStream_t st) {
   // 1. preprocess
-  const int n_rows = p.B * p.Hq * p.Sq_pad;
+  const int64_t n_rows64 = (int64_t)p.B * p.Hq * p.Sq_pad;
   const int threads = 256;
+  // The scalar preprocess spends a warp per row: its grid is the larger one.
+  if (n_rows64 * 32 / threads + 1 > 0x7fffffffLL) {
+    set_last_error("ffa_bwd: B * Hq * round_up(Sq, 128) rows exceed the preprocess grid limit");
+    return FFA_ERR_UNSUPPORTED;
+  }
+  const int n_rows = (int)n_rows64;
   const bool vec = ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout)) & 15) == 0 &&
                    o_str[0] % 8 == 0 && o_str[1] % 8 == 0 && o_str[2] % 8 == 0 && do_str[0] % 8 == 0 &&
                    do_str[1] % 8 == 0 && do_str[2] % 8 == 0;
@@ -1032,7 +1033,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
         reinterpret_cast<const T*>(o), reinterpret_cast<const T*>(dout), lse, lse2, delta, p.Hq, p.Sq, p.Sq_pad,
         o_str[0], o_str[1], o_str[2], do_str[0], do_str[1], do_str[2], n_rows);
   } else {
-    const int blocks = (n_rows * 32 + threads - 1) / threads;
+    const int blocks = (int)(((int64_t)n_rows * 32 + threads - 1) / threads);
     ffa_bwd_pre_kernel<T><<<blocks, threads, 0, st>>>(
         reinterpret_cast<const T*>(o), reinterpret_cast<const T*>(dout), lse, lse2, delta, p.Hq, p.Sq, p.Sq_pad,
         DV, o_str[0], o_str[1], o_str[2], do_str[0], do_str[1], do_str[2], n_rows);
@@ -1042,11 +1043,8 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
   // 2. dK / dV
   {
     auto kern = ffa_bwd_dkdv_kernel<T, D, DV>;
-    static bool set = false;
-    if (!set) {
-      if ((s = set_smem(kern, DkdvCfg<D, DV>::SMEM))) return s;
-      set = true;
-    }
+    static std::atomic<uint64_t> done{0};
+    if ((s = smem_attr_once(kern, DkdvCfg<D, DV>::SMEM, done))) return s;
     const int grid = (p.Skv + BWD_BT - 1) / BWD_BT * p.B * p.Hkv;
     kern<<<grid, BWD_THREADS, DkdvCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;
@@ -1054,11 +1052,8 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
   // 3. dQ
   {
     auto kern = ffa_bwd_dq_kernel<T, D, DV>;
-    static bool set = false;
-    if (!set) {
-      if ((s = set_smem(kern, DqCfg<D, DV>::SMEM))) return s;
-      set = true;
-    }
+    static std::atomic<uint64_t> done{0};
+    if ((s = smem_attr_once(kern, DqCfg<D, DV>::SMEM, done))) return s;
     const int grid = (p.Sq + BWD_BT - 1) / BWD_BT * p.B * p.Hq;
     kern<<<grid, BWD_THREADS, DqCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
     if ((s = launch_status())) return s;

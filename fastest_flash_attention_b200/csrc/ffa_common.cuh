@@ -95,8 +95,11 @@ __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
 // `*abort` is raised so every other role of the CTA stops waiting too, and
 // false is returned.  A raised `*abort` makes every later wait return false
 // immediately, unless `drain` is set: draining waits (for copies or MMAs still
-// in flight before the CTA releases its memory) ignore the abort flag but are
-// still bounded by the same limit.
+// in flight before the CTA releases its memory) ignore the abort flag and are
+// bounded by at least kDrainFloorNs whatever the caller's limit, so a short
+// user limit can never let a CTA free shared memory or TMEM under a copy or
+// an MMA that is still running.
+constexpr unsigned long long kDrainFloorNs = 4000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const ErrCtx& ec,
                                           volatile int* abort, uint32_t site, bool drain = false) {
   if (mbar_test(bar, parity)) return true;
@@ -104,7 +107,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   // The limit is counted in SM clock cycles (cheap to read); 2 cycles per ns
   // over-approximates every B200 clock, so the wall-clock bound still holds.
   const long long t0 = clock64();
-  const long long limit = (long long)(ec.limit_ns * 2ull);
+  const unsigned long long lim_ns =
+      (drain && ec.limit_ns < kDrainFloorNs) ? kDrainFloorNs : ec.limit_ns;
+  const long long limit = (long long)(lim_ns * 2ull);
   uint32_t spins = 0;
   while (true) {
     if (mbar_test(bar, parity)) return true;
@@ -368,29 +373,6 @@ __device__ __forceinline__ float2 tanh_small2(float2 x) {
   p = ffma2(p, x2, f2(1.3333333333333333e-1f));
   p = ffma2(p, x2, f2(-3.3333333333333333e-1f));
   return ffma2(fmul2(p, x2), x, x);
-}
-
-// 2^x on the FMA pipe, for two lanes at once, to offload the MUFU unit.
-// x = n + f with n = rint(x) (magic-constant rounding), f in [-1/2, 1/2];
-// 2^f by a cubic whose coefficients are the relative-error minimax fit from
-// csrc/fit_exp2_poly.py (Remez exchange; max relative error 7.5e-5); 2^n is
-// applied by adding n to the exponent field.  Inputs below -126 return 0.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  // Below -126 the result would be a denormal: flush to 0 like ex2.approx.ftz
-  // (and keep -inf -> exactly 0, which masked scores rely on).
-  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
-  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
-  const float2 t = fadd2(xc, magic);                       // low mantissa bits hold rint(x)
-  const float2 n = fadd2(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = ffma2(n, make_float2(-1.f, -1.f), xc);  // x - n in [-1/2, 1/2]
-  float2 p = make_float2(5.517166853e-02f, 5.517166853e-02f);
-  p = ffma2(p, f, make_float2(2.426111251e-01f, 2.426111251e-01f));
-  p = ffma2(p, f, make_float2(6.932609677e-01f, 6.932609677e-01f));
-  p = ffma2(p, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
-  float2 r;
-  r.x = x.x < -126.f ? 0.f : __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
-  r.y = x.y < -126.f ? 0.f : __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
-  return r;
 }
 
 // tanh on |x| <= 1/2 by its Taylor series to x^11 (odd terms; coefficients

@@ -542,12 +542,8 @@ static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
                       int grid, cudaStream_t stream) {
   using Cfg = FwdCfg<D, DV>;
   auto kern = ffa_fwd_kernel<T, D, DV>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    if (st) return st;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (int st = smem_attr_once(kern, Cfg::SMEM, attr_done)) return st;
   kern<<<grid, FWD_THREADS, Cfg::SMEM, stream>>>(mq, mk, mv, p);
   return launch_status();
 }

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "ffa_b200.h"
 
 namespace ffa {
@@ -30,6 +32,23 @@ inline int launch_status() { return cuda_status(cudaGetLastError()); }
 int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint32_t elem_bytes, uint64_t d0,
                  uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1_bytes, uint64_t s2_bytes, uint64_t s3_bytes,
                  uint32_t b0, uint32_t b1);
+
+// Raises a kernel's dynamic shared-memory limit once per device.  The
+// attribute belongs to the device's context, so the "done" record is a bit
+// per device; the record is atomic because entry points may be called from
+// several host threads (setting the attribute twice is harmless).
+template <typename Kernel>
+int smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  int s = cuda_status(cudaGetDevice(&dev));
+  if (s) return s;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return FFA_OK;
+  s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (s) return s;
+  if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return FFA_OK;
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
