@@ -158,6 +158,14 @@ def err_word(device: torch.device) -> torch.Tensor:
     return w
 
 
+# Error-word codes that report invalid input data rather than an expired wait.
+_DATA_ERRORS = {
+    0x1FF: "block mask keeps more key tiles than the forward kernel's tile list holds",
+    0x3E0: "paged decode: a context length is negative or exceeds max_pages_per_req * page_size",
+    0x3E1: "paged decode: a block-table entry is outside [0, num_pages)",
+}
+
+
 def sync_check_enabled() -> bool:
     return os.environ.get("FFA_SYNC_CHECK", "0") not in ("", "0")
 
@@ -172,6 +180,8 @@ def check_device_errors(device: torch.device | None = None) -> None:
         code = int(w.item())
         if code != 0:
             w.zero_()
+            if code in _DATA_ERRORS:
+                raise RuntimeError(f"FFA_ERR_INVALID_ARG: {_DATA_ERRORS[code]} (device code 0x{code:x}) on cuda:{idx}")
             raise RuntimeError(f"FFA_ERR_DEVICE_TIMEOUT: in-kernel wait expired at site 0x{code:x} on cuda:{idx}")
 
 

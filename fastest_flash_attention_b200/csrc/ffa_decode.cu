@@ -39,6 +39,8 @@ struct DecParams {
   const int* block_table;
   int64_t bt_stride;  // elements between requests' rows of the block table
   const int* ctx_lens;
+  int num_pages;      // valid page ids are [0, num_pages)
+  int max_ctx;        // max_pages_per_req * page_size
   float* o_part;      // [R, max_splits, Hq, D]
   float* lse_part;    // [R, max_splits, Hq] (base 2)
   int R, Hq, Hkv, G, page_size, max_splits, chunks_per_split;
@@ -49,6 +51,10 @@ struct DecParams {
 };
 
 enum : uint32_t { SITE_DEC_FULL = 0x301, SITE_DEC_EMPTY = 0x302 };
+// Invalid paging data (not expired waits): a context length outside
+// [0, max_pages_per_req * page_size], or a block-table entry outside
+// [0, num_pages).  The offending CTA records the code and loads nothing.
+enum : uint32_t { SITE_DEC_BAD_CTX = 0x3E0, SITE_DEC_BAD_PAGE = 0x3E1 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -111,6 +117,10 @@ __global__ void __launch_bounds__(DEC_THREADS)
 
   const int split = blockIdx.x, r = blockIdx.y, h = blockIdx.z;
   const int ctx = p.ctx_lens[r];
+  if (ctx < 0 || ctx > p.max_ctx) {
+    if (split == 0 && h == 0 && threadIdx.x == 0 && p.ec.err) atomicCAS(p.ec.err, 0u, SITE_DEC_BAD_CTX);
+    return;
+  }
   const int n_chunks = (ctx + DEC_CHUNK - 1) / DEC_CHUNK;
   const int c_begin = split * p.chunks_per_split;
   if (c_begin >= n_chunks) return;  // this request has fewer splits
@@ -140,6 +150,11 @@ __global__ void __launch_bounds__(DEC_THREADS)
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.ec, abort_flag, SITE_DEC_EMPTY)) break;
         const int c = c_begin + idx;
         const int page = table[c / sub_per_page];
+        if ((unsigned)page >= (unsigned)p.num_pages) {
+          if (p.ec.err) atomicCAS(p.ec.err, 0u, SITE_DEC_BAD_PAGE);
+          *abort_flag = 1;
+          break;
+        }
         const int row = (page * p.Hkv + h) * p.page_size + (c % sub_per_page) * DEC_CHUNK;
         mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
         uint8_t* dst = smem + s * Cfg::STAGE;
@@ -324,7 +339,9 @@ __global__ void ffa_decode_merge_kernel(const float* __restrict__ o_part, const 
   if (wid >= R * Hq) return;
   const int r = wid / Hq, head = wid % Hq;
   const int n_chunks = (ctx_lens[r] + DEC_CHUNK - 1) / DEC_CHUNK;
-  const int ns = (n_chunks + chunks_per_split - 1) / chunks_per_split;
+  // clamped: an out-of-range length (reported by the split kernel) never
+  // makes the merge read past the request's partials
+  const int ns = min(max((n_chunks + chunks_per_split - 1) / chunks_per_split, 0), max_splits);
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, lse_part[((int64_t)r * max_splits + s) * Hq + head]);
   float L = 0.f;
@@ -358,12 +375,8 @@ static int launch_decode(const CUtensorMap& mk, const CUtensorMap& mv, const Dec
                          float* lse, int64_t o_sr, int64_t o_sh, cudaStream_t st) {
   using Cfg = DecCfg<D>;
   auto kern = ffa_paged_decode_kernel<T, D>;
-  static bool set = false;
-  if (!set) {
-    int s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    if (s) return s;
-    set = true;
-  }
+  static std::atomic<uint64_t> done{0};
+  if (int s = smem_attr_once(kern, Cfg::SMEM, done)) return s;
   dim3 grid(p.max_splits, p.R, p.Hkv);
   kern<<<grid, DEC_THREADS, Cfg::SMEM, st>>>(mk, mv, p);
   int s = launch_status();
@@ -394,6 +407,8 @@ struct MlaParams {
   const int* block_table;
   int64_t bt_stride;
   const int* ctx_lens;
+  int num_pages;  // valid page ids are [0, num_pages)
+  int max_ctx;    // max_pages_per_req * page_size
   float* o_part;    // [R, max_splits, H, 512]
   float* lse_part;  // [R, max_splits, H] (base 2)
   int R, H, page_size, max_splits, chunks_per_split;
@@ -479,7 +494,7 @@ __global__ void __launch_bounds__(128) ffa_mla_merge_kernel(const float* __restr
                                                             int chunks_per_split, int64_t o_sr, int64_t o_sh) {
   const int r = blockIdx.x / H, head = blockIdx.x % H;
   const int n_chunks = (ctx_lens[r] + DEC_CHUNK - 1) / DEC_CHUNK;
-  const int ns = (n_chunks + chunks_per_split - 1) / chunks_per_split;
+  const int ns = min(max((n_chunks + chunks_per_split - 1) / chunks_per_split, 0), max_splits);
   const int64_t base = (int64_t)r * max_splits * H + head;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, lse_part[base + (int64_t)s * H]);
@@ -516,6 +531,10 @@ __global__ void __launch_bounds__(MLT_THREADS, 1)
 
   const int split = blockIdx.x, r = blockIdx.y;
   const int ctx = p.ctx_lens[r];
+  if (ctx < 0 || ctx > p.max_ctx) {
+    if (split == 0 && threadIdx.x == 0 && p.ec.err) atomicCAS(p.ec.err, 0u, SITE_DEC_BAD_CTX);
+    return;
+  }
   const int n_chunks = (ctx + DEC_CHUNK - 1) / DEC_CHUNK;
   const int c_begin = split * p.chunks_per_split;
   if (c_begin >= n_chunks) return;
@@ -562,7 +581,16 @@ __global__ void __launch_bounds__(MLT_THREADS, 1)
     const int n_blk = (ctx + br - 1) / br;  // br-row blocks holding the request's tokens
     int win = -1, pid = 0;  // page window [32 win, 32 win + 32) held by the lanes
     int issued = 0;
-    bool ok = true;
+    // Every page id this split will read is checked before the first copy is
+    // armed (independent loads, one latency); a bad id stops the CTA.
+    const int page_last = min(n_pages_req, (c_begin * DEC_CHUNK + n_tiles * MLT_TILE + p.page_size - 1) / p.page_size);
+    bool bad = false;
+    for (int i = page0 + lane; i < page_last; i += 32) bad |= (unsigned)table[i] >= (unsigned)p.num_pages;
+    bool ok = !__any_sync(0xffffffffu, bad);
+    if (!ok) {
+      if (lane == 0 && p.ec.err) atomicCAS(p.ec.err, 0u, SITE_DEC_BAD_PAGE);
+      *abort_flag = 1;
+    }
     for (int t = 0; t < n_tiles && ok; ++t) {
       for (int kk = 0; kk < MLT_NSLOT && ok; ++kk) {
         const int k = (kk + MLT_NSLOT - 1) % MLT_NSLOT;  // the rope slot first: it frees earliest
@@ -861,6 +889,9 @@ extern "C" int ffa_paged_decode(const void* q, const void* k_pages, const void* 
   p.block_table = block_table;
   p.bt_stride = max_pages_per_req;
   p.ctx_lens = ctx_lens;
+  p.num_pages = num_pages;
+  if ((int64_t)max_pages_per_req * page_size > 0x7fffffffLL) return FFA_ERR_UNSUPPORTED;
+  p.max_ctx = max_pages_per_req * page_size;
   const int max_chunks = max_pages_per_req * (page_size / DEC_CHUNK);
   p.max_splits = (max_chunks + chunks_per_split - 1) / chunks_per_split;
   uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 127) & ~uintptr_t(127);
@@ -932,6 +963,9 @@ extern "C" int ffa_mla_decode(const void* q, const void* ckv_pages, const int* b
   p.block_table = block_table;
   p.bt_stride = max_pages_per_req;
   p.ctx_lens = ctx_lens;
+  p.num_pages = num_pages;
+  if ((int64_t)max_pages_per_req * page_size > 0x7fffffffLL) return FFA_ERR_UNSUPPORTED;
+  p.max_ctx = max_pages_per_req * page_size;
   const int max_chunks = max_pages_per_req * (page_size / DEC_CHUNK);
   p.max_splits = (max_chunks + chunks_per_split - 1) / chunks_per_split;
   if (p.max_splits > 65535 || R > 65535) return FFA_ERR_UNSUPPORTED;
@@ -959,13 +993,8 @@ extern "C" int ffa_mla_decode(const void* q, const void* ckv_pages, const int* b
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto launch = [&](auto kern, auto merge) -> int {
-    static bool set_b = false, set_h = false;
-    bool& set = (dtype == FFA_DTYPE_BF16) ? set_b : set_h;
-    if (!set) {
-      int e = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MLT_SMEM));
-      if (e) return e;
-      set = true;
-    }
+    static std::atomic<uint64_t> done_b{0}, done_h{0};
+    if (int e = smem_attr_once(kern, MLT_SMEM, dtype == FFA_DTYPE_BF16 ? done_b : done_h)) return e;
     kern<<<dim3(p.max_splits, R), MLT_THREADS, MLT_SMEM, s>>>(mc, p);
     int e = launch_status();
     if (e) return e;

@@ -27,6 +27,29 @@ def default_chunks_per_split(ctx_max: int, R: int, Hkv: int, num_sms: int = 148)
     return max(16, min(128, math.ceil(chunks / splits)))
 
 
+def check_block_table(block_table: torch.Tensor, ctx_lens: torch.Tensor, num_pages: int, page_size: int) -> None:
+    """Host-side validation of paging data (CPU tensors): every context length
+    in [0, width * page_size] and every page id a request reads in
+    [0, num_pages).  Raises ValueError naming the first bad request.  The
+    decode kernels repeat these checks on the device (reporting through the
+    error word) for tables that never pass through the host."""
+    bt = block_table.to("cpu", torch.int64)
+    lens = ctx_lens.to("cpu", torch.int64)
+    if bt.dim() != 2 or lens.dim() != 1 or lens.numel() != bt.shape[0]:
+        raise ValueError("block_table must be [R, max_pages] and ctx_lens [R]")
+    width = bt.shape[1]
+    bad_len = (lens < 0) | (lens > width * page_size)
+    if bool(bad_len.any()):
+        r = int(bad_len.nonzero()[0, 0])
+        raise ValueError(f"ctx_lens[{r}] = {int(lens[r])} is outside [0, {width * page_size}] "
+                         f"({width} pages of {page_size} tokens)")
+    used = (torch.arange(width)[None, :] * page_size) < lens[:, None]  # pages each request reads
+    bad = used & ((bt < 0) | (bt >= num_pages))
+    if bool(bad.any()):
+        r, c = (int(x) for x in bad.nonzero()[0])
+        raise ValueError(f"block_table[{r}, {c}] = {int(bt[r, c])} is outside [0, {num_pages})")
+
+
 def paged_decode(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor, block_table: torch.Tensor,
                  ctx_lens: torch.Tensor, *, scale: Optional[float] = None, softcap: Optional[float] = None,
                  return_lse: bool = False, chunks_per_split: Optional[int] = None, max_ctx: Optional[int] = None):

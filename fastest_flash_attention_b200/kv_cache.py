@@ -20,6 +20,7 @@ from typing import List, Optional, Sequence, Tuple
 import torch
 
 from . import _lib
+from .decode import check_block_table
 
 
 class ContinuousKVCache:
@@ -169,6 +170,7 @@ class PagedKVCache:
             if t:
                 bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
         lens = torch.tensor([self.sequences[s]["len"] for s in seq_ids], dtype=torch.int32)
+        check_block_table(bt, lens, self.max_pages, self.page_size)
         return bt.to(device), lens.to(device)
 
     def decode(self, q: torch.Tensor, seq_ids: Sequence[int], *, scale: Optional[float] = None,

@@ -26,6 +26,7 @@ from typing import List, Optional, Sequence
 import torch
 
 from . import _lib
+from .decode import check_block_table
 
 
 def mla_chunks_per_split(ctx_max: int, R: int, num_sms: int = 148) -> int:
@@ -125,6 +126,7 @@ class MLALatentCache:
         for i, t in enumerate(tables):
             bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
         lens = torch.tensor([self.sequences[s]["len"] for s in seq_ids], dtype=torch.int32)
+        check_block_table(bt, lens, self.pages.shape[0], self.page_size)
         return bt.to(self.pages.device), lens.to(self.pages.device)
 
 

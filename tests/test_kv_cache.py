@@ -48,3 +48,22 @@ def test_continuous_cache_append():
     k, v = c.append(a * 2, a)
     assert k.shape == (2, 2, 6, 8) and torch.equal(k[:, :, 3:], a * 2)
     assert c.seq_lens.tolist() == [6, 6]
+
+
+def test_block_table_validation_rejects_bad_paging_data():
+    import pytest
+    from fastest_flash_attention_b200.decode import check_block_table
+    bt = torch.tensor([[3, 1, 0], [2, 0, 0]], dtype=torch.int32)
+    check_block_table(bt, torch.tensor([9, 4], dtype=torch.int32), num_pages=4, page_size=4)  # valid
+    # a page id that the request reads is out of the pool
+    with pytest.raises(ValueError, match=r"block_table\[0, 0\] = 3 is outside \[0, 3\)"):
+        check_block_table(bt, torch.tensor([9, 4], dtype=torch.int32), num_pages=3, page_size=4)
+    # unused trailing entries are not read, so they are not checked
+    check_block_table(torch.tensor([[1, -7]], dtype=torch.int32), torch.tensor([4], dtype=torch.int32), 2, 4)
+    with pytest.raises(ValueError, match=r"block_table\[0, 1\] = -7"):
+        check_block_table(torch.tensor([[1, -7]], dtype=torch.int32), torch.tensor([5], dtype=torch.int32), 2, 4)
+    # lengths beyond what the table row covers, or negative
+    with pytest.raises(ValueError, match=r"ctx_lens\[1\] = 13 is outside \[0, 12\]"):
+        check_block_table(bt, torch.tensor([9, 13], dtype=torch.int32), num_pages=4, page_size=4)
+    with pytest.raises(ValueError, match=r"ctx_lens\[0\] = -1"):
+        check_block_table(bt, torch.tensor([-1, 0], dtype=torch.int32), num_pages=4, page_size=4)
