@@ -23,7 +23,27 @@ from .config import AttentionConfig
 from .utils import auto_select_block_size, maybe_unsqueeze_head
 
 _KERNEL_DTYPES = (torch.float16, torch.bfloat16)
-FWD_HEAD_DIMS = ((64, 64), (128, 128), (192, 128))  # forward (qk, v)
+FWD_HEAD_DIMS = ((64, 64), (128, 128), (192, 128))  # kernel instantiations (qk, v)
+MAX_HEAD_DIM = 192  # qk head dim; v head dim up to 128
+
+
+def kernel_head_dims(D: int, Dv: int) -> Optional[Tuple[int, int]]:
+    """Smallest kernel instantiation (qk, v) that holds head dims (D, Dv), or
+    None.  Other head dims (the reference computes any D) run on a kernel
+    whose tile is wider: q/k (and v) are zero-padded in the head dim, which
+    leaves every dot product, the softmax and the kept output columns
+    unchanged; the caller's scale (default 1/sqrt(D) of the true D) is passed
+    through unchanged."""
+    for kd, kv in FWD_HEAD_DIMS:
+        if D <= kd and Dv <= kv:
+            return kd, kv
+    return None
+
+
+def _pad_last(t: torch.Tensor, width: int) -> torch.Tensor:
+    if t.shape[-1] == width:
+        return t
+    return torch.nn.functional.pad(t, (0, width - t.shape[-1]))
 
 
 def kernel_dtype(t: torch.Tensor, compute_dtype: Optional[torch.dtype] = None) -> torch.dtype:
@@ -66,10 +86,17 @@ def flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
         raise ValueError(f"incompatible q/k/v shapes {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
     if Hq % Hkv != 0:
         raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
-    if (D, Dv) not in FWD_HEAD_DIMS:
+    kdims = kernel_head_dims(D, Dv)
+    if kdims is None:
         raise ValueError(f"head dims (qk={D}, v={Dv}) not supported by the sm_100a forward kernel "
-                         f"(supported: {FWD_HEAD_DIMS})")
+                         f"(supported: qk <= {MAX_HEAD_DIM}, v <= 128)")
     dt = kernel_dtype(q, compute_dtype)
+    if kdims != (D, Dv):
+        o, lse = flash_fwd(_pad_last(q.to(dt), kdims[0]), _pad_last(k.to(dt), kdims[0]),
+                           _pad_last(v.to(dt), kdims[1]), scale=scale, causal=causal, q_offset=q_offset,
+                           window=window, softcap=softcap, block_mask=block_mask, mask_block=mask_block,
+                           compute_dtype=compute_dtype, want_lse=want_lse)
+        return o[..., :Dv], lse
     q = _tma_ready(q, dt)
     k = _tma_ready(k, dt)
     v = _tma_ready(v, dt)
@@ -188,12 +215,21 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     _lib.require_cuda(dout, q, k, v, o, lse)
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
-    if (D, v.shape[3]) not in FWD_HEAD_DIMS or o.shape[3] != v.shape[3] or dout.shape[3] != v.shape[3]:
-        raise ValueError(f"head dims (qk={D}, v={v.shape[3]}) not supported by the sm_100a backward kernel "
-                         f"(supported: {FWD_HEAD_DIMS})")
+    Dv = v.shape[3]
+    kdims = kernel_head_dims(D, Dv)
+    if kdims is None or o.shape[3] != Dv or dout.shape[3] != Dv:
+        raise ValueError(f"head dims (qk={D}, v={Dv}) not supported by the sm_100a backward kernel "
+                         f"(supported: qk <= {MAX_HEAD_DIM}, v <= 128)")
     if Hq % Hkv != 0:
         raise ValueError(f"query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
     dt = kernel_dtype(q, compute_dtype)
+    if kdims != (D, Dv):
+        # zero columns: Delta, dP and the kept gradient columns are unchanged
+        kd, kv = kdims
+        dq, dk, dv = flash_bwd(_pad_last(dout.to(dt), kv), _pad_last(q.to(dt), kd), _pad_last(k.to(dt), kd),
+                               _pad_last(v.to(dt), kv), _pad_last(o.to(dt), kv), lse, scale=scale, causal=causal,
+                               q_offset=q_offset, window=window, softcap=softcap, compute_dtype=compute_dtype)
+        return dq[..., :D], dk[..., :D], dv[..., :Dv]
     q, k, v, o, dout = (_tma_ready(t, dt) for t in (q, k, v, o, dout))
     if lse.dim() == 4:
         lse = lse[..., 0]

@@ -82,6 +82,9 @@ def _oracle_grads(q, k, v, do, hq, **kw):
     (1, 4, 1, 257, 64, True, 100, None),       # MQA + window
     (1, 2, 2, 384, 128, True, 130, 30.0),      # config-3 features
     (2, 2, 2, 200, 64, False, None, None),
+    (1, 2, 1, 150, 16, True, None, None),      # head dims without their own kernel: zero-padded
+    (1, 2, 2, 170, 32, True, 50, 20.0),
+    (1, 2, 2, 129, 96, False, None, None),
 ])
 def test_backward_vs_oracle(B, Hq, Hkv, S, D, causal, window, softcap):
     q, k, v, do = _rand(B, Hq, S, D, seed=1), _rand(B, Hkv, S, D, seed=2), _rand(B, Hkv, S, D, seed=3), \

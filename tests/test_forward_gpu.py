@@ -36,7 +36,7 @@ def close(a, b, tol, what):
     assert err <= tol, f"{what}: max abs err {err:.3e} > {tol}"
 
 
-GOLDEN_FWD = ["fwd_causal_d64", "fwd_causal_d128_ragged", "fwd_window_d64", "fwd_softcap_d64", "fwd_gqa_d128",
+GOLDEN_FWD = ["fwd_basic_d16", "fwd_causal_d64", "fwd_causal_d128_ragged", "fwd_window_d64", "fwd_softcap_d64", "fwd_gqa_d128",
               "fwd_noncausal_sq_ne_skv_d64", "fwd_two_pass_d64", "fwd_blockmask_d64"]
 
 
@@ -63,6 +63,31 @@ def test_forward_kvcache_golden():
                                               kv_cache=(dev(g["k_cache"]), dev(g["v_cache"])), return_lse=True)
     close(o, g["o"], O_TOL, "O")
     close(lse, g["lse"], LSE_TOL, "LSE")
+
+
+def test_forward_compute_dtype_fp16_golden():
+    """fp32 callers with compute_dtype=torch.float16 (cpu_reference.py:28-32,
+    260-261): the kernels run in fp16 and the output comes back in fp32."""
+    g = load_golden("fwd_fp16_compute_d16")
+    p = golden_params_dtype(g)
+    assert p["compute_dtype"] == torch.float16
+    q, k, v = (dev(g[x], torch.float32) for x in ("q", "k", "v"))
+    o, lse = ffa().fastest_flash_attn_forward(q, k, v, block_size=p["block_size"], compute_dtype=torch.float16,
+                                              return_lse=True)
+    assert o.dtype == torch.float32
+    close(o, g["o"], O_TOL, "O")
+    close(lse, g["lse"], LSE_TOL, "LSE")
+    # the same through an AttentionConfig
+    cfg = ffa().AttentionConfig(compute_dtype=torch.float16, return_lse=True)
+    o2, _ = ffa().fastest_flash_attn_forward(q, k, v, config=cfg)
+    assert torch.equal(o, o2)
+
+
+def golden_params_dtype(g):
+    import ast
+    txt = str(g["params"]).replace("torch.float16", "'float16'").replace("torch.bfloat16", "'bfloat16'")
+    p = ast.literal_eval(txt)
+    return {k: getattr(torch, v) if k == "compute_dtype" else v for k, v in p.items()}
 
 
 def _rand(*shape, dtype=torch.bfloat16, scale=1.0, seed=0):
@@ -101,6 +126,33 @@ def test_forward_vs_oracle(B, Hq, Hkv, Sq, Skv, D, causal, window, softcap):
     got = lse.float().cpu().numpy()
     assert np.isneginf(got[empty]).all()
     close(got[~empty], rl[~empty], LSE_TOL, "LSE")
+
+
+@pytest.mark.parametrize("D,Dv,causal,window", [
+    (16, 16, True, None), (32, 32, True, 40), (8, 8, False, None), (80, 80, True, None), (96, 64, False, None),
+    (160, 128, True, None), (100, 100, True, 77),
+])
+def test_forward_other_head_dims(D, Dv, causal, window):
+    """Head dims without their own kernel run zero-padded on the next wider one
+    (the reference is shape-generic; its own tests use D = 4/8/16)."""
+    B, Hq, Hkv, S = 1, 4, 2, 203
+    q = _rand(B, Hq, S, D, seed=21)
+    k = _rand(B, Hkv, S, D, seed=22)
+    v = _rand(B, Hkv, S, Dv, seed=23)
+    o, lse = ffa().fastest_flash_attn_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal, sliding_window=window,
+                                              return_lse=True)
+    assert o.shape == (B, Hq, S, Dv)
+    ro, rl = _oracle_fwd(q, k, v, causal=causal, sliding_window=window, block_q=128, block_kv=128)
+    close(o, ro, O_TOL, "O")
+    close(lse, rl, LSE_TOL, "LSE")
+
+
+def test_unsupported_head_dims_raise():
+    for D, Dv in ((256, 256), (64, 160), (200, 128)):
+        q = torch.zeros(1, 1, 8, D, device="cuda", dtype=torch.bfloat16)
+        v = torch.zeros(1, 1, 8, Dv, device="cuda", dtype=torch.bfloat16)
+        with pytest.raises(ValueError, match="not supported"):
+            ffa().fastest_flash_attn_forward(q, q, v)
 
 
 def test_3d_input_and_fp32_input():

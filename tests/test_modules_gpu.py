@@ -143,3 +143,33 @@ def test_mla_module_training_backward():
     assert rel(y, y2.detach().float().cpu().numpy()) <= 3e-2
     assert rel(gx, x2.grad.float().cpu().numpy()) <= 5e-2
     assert rel(gw, mod.q_proj.weight.grad.float().cpu().numpy()) <= 5e-2
+
+
+def test_mla_prefill_config5_full_size_rows():
+    """Config 5 at full size: FastestFlashMLA hidden 4096, 32 heads, latent 512,
+    rope 64, B=16, S=4096, weights N(0, 0.02), bf16, causal prefill
+    (modules/flash_mla.py:116-172).  Output rows of every batch element are
+    checked against the same module with attention recomputed in fp32 torch
+    over all 32 heads for those rows."""
+    m = ffa()
+    torch.manual_seed(5)
+    mod = m.FastestFlashMLA(hidden_size=4096, num_heads=32, head_dim=128, latent_dim=512, rope_dim=64).cuda().eval()
+    for prm in mod.parameters():
+        torch.nn.init.normal_(prm, std=0.02)
+    mod = mod.to(torch.bfloat16)
+    B, S = 16, 4096
+    x = torch.randn(B, S, 4096, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        y = mod(x)
+        q, k, v = mod.qkv(x)
+        worst = 0.0
+        for b in range(B):
+            rows = torch.arange(b * 37 % 97, S, 397, device="cuda")
+            s = (q[b][:, rows].float() @ k[b].float().transpose(-1, -2)) * mod.scale  # [H, n, S]
+            s = s.masked_fill(torch.arange(S, device="cuda")[None, None, :] > rows[None, :, None], float("-inf"))
+            o = torch.softmax(s, -1) @ v[b].float()                                   # [H, n, 128]
+            o = torch.nn.functional.pad(o, (0, mod.rope_dim)).to(torch.bfloat16)
+            y_ref = mod.o_proj(o.transpose(0, 1).reshape(rows.numel(), -1)).float()
+            err = (y[b, rows].float() - y_ref).abs().max().item() / y_ref.abs().max().item()
+            worst = max(worst, err)
+    assert worst <= 2e-2, worst
