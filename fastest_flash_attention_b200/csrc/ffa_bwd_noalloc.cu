@@ -14,6 +14,8 @@
 //    length rounded up to 128) rows; larger problems are rejected with
 //    FFA_ERR_UNSUPPORTED.  Every GPU that loads the library keeps this array
 //    (8 MiB + 256 B) for the life of the process.
+//  * Only D == Dv is served (query/key and value head dims equal); the
+//    MLA training shape (192, 128) needs ffa_bwd with a workspace.
 //  * All calls on a device share the one array.  Each call overwrites every
 //    scratch row it later reads, so nothing needs clearing between calls, but
 //    calls whose kernels overlap on the GPU (different streams, or different

@@ -6,7 +6,7 @@
  * throws, never allocates device memory, and returns an ffa_status.  Tensors
  * are row-major in their last dimension (stride 1); the other strides are in
  * elements.  The library is loaded by the Python package through ctypes and
- * can be bound the same way from any FFI.
+ * can be bound the same way from any FFI (ctypes, cgo, JNI, N-API).
  *
  * Reference interfaces replaced (MindIntels/fastest_flash_attention, paths
  * relative to the project root):
@@ -109,7 +109,9 @@ int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const
  * point exists for callers that cannot allocate device memory (code handed
  * only its input/output buffers by a host framework, or hosts that forbid a
  * device-synchronising cudaMalloc in the middle of a step).  Same arguments
- * and results as ffa_bwd without the workspace: the scratch rows live in an
+ * and bit-identical results as ffa_bwd without the workspace and with Dv
+ * fixed to D (so only D == Dv; the MLA shape D=192, Dv=128 is rejected with
+ * FFA_ERR_UNSUPPORTED and needs ffa_bwd): the scratch rows live in an
  * array compiled into the library (8 MiB + 256 B held by every GPU that loads
  * it, until process exit).  Limit: B * Hq * round_up(Sq, 128) <=
  * FFA_BWD_NOALLOC_MAX_ROWS, else FFA_ERR_UNSUPPORTED.  All calls on a device
