@@ -8,9 +8,11 @@ is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs one process per GPU (torchrun); every rank processes its own full
-batch (weak scaling, no collective on the data path) and rank 0 prints the
-whole-job aggregate over the max-over-ranks time.
+N > 1 runs one process per GPU (torchrun); the one config-2 job is split by
+its 32 (batch, kv-head) GQA groups across the ranks (strong scaling, no
+collective on the data path) and rank 0 prints the whole-job throughput over
+the max-over-ranks time.  N > 1 adds two lines: config 4 decode split by
+request (greedy LPT on context length) and the sequence-sharded ring.
 
 --impl reference times the reference's CPU algorithm (the numpy port in
 oracle/, the reference being a Python package that cannot travel) on the
@@ -54,10 +56,13 @@ def fwd_flops(B, Hq, S, D) -> float:
 
 
 def workload_config(n_gpus: int) -> dict:
+    groups = CFG["B"] * CFG["Hkv"]
     return {
         "workload": "GQA causal prefill forward (O + LSE)",
-        "batch_per_gpu": CFG["B"], "q_heads": CFG["Hq"], "kv_heads": CFG["Hkv"], "seq_len": CFG["S"],
-        "head_dim": CFG["D"], "causal": True, "parallelism": f"shard-by-batch x{n_gpus} (no collective)",
+        "batch": CFG["B"], "q_heads": CFG["Hq"], "kv_heads": CFG["Hkv"], "seq_len": CFG["S"],
+        "head_dim": CFG["D"], "causal": True,
+        "parallelism": f"{groups} (batch, kv-head) GQA groups split over {n_gpus} GPU(s), "
+                       f"{groups // n_gpus}-{-(-groups // n_gpus)} per GPU, no collective on the data path",
         "l2": "inputs 403 MB per GPU > 126 MB L2, no flush needed",
         "flop_convention": "4*D*causal_pairs*B*Hq (exact unmasked pairs)",
     }
@@ -203,7 +208,7 @@ def run_reference(args, world, rank):
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)*D^-1/4, bf16-rounded)",
         "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
@@ -302,6 +307,19 @@ def secondary_lines(dev, peaks, peak_src):
         "ms": d_ms, "gbs": byts / d_ms / 1e6, "frac_of_hbm": byts / d_ms / 1e6 / hbm,
         "bytes": byts, "peak": f"{hbm} GB/s ({peak_src})"}
     del q, kp, vp
+    # config 5 prefill: the MLA module's attention at (qk 192, v 128), B=16 H=32 S=4096 causal
+    B5, H5, S5 = 16, 32, 4096
+    g = torch.Generator(device=dev).manual_seed(5)
+    q = torch.randn(B5, H5, S5, 192, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B5, H5, S5, 192, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B5, H5, S5, 128, device=dev, generator=g).to(torch.bfloat16)
+    p_ms = _time(lambda: flash_fwd(q, k, v, scale=192 ** -0.5, causal=True), 10, dev)
+    pf = 2.0 * (192 + 128) * causal_pairs(S5) * B5 * H5
+    out["mla_prefill_cfg5"] = {
+        "workload": "config 5 prefill attention: B=16 H=32 S=4096 causal, qk 192 / v 128 (unpadded V), bf16",
+        "ms": p_ms, "tflops": pf / p_ms / 1e9, "frac_of_peak": pf / p_ms / 1e9 / pk,
+        "flops": pf, "peak": f"{pk} TFLOP/s ({peak_src} bf16)"}
+    del q, k, v
     # config 5: MLA absorbed decode step, B=16 at context 4096 (latent 512 + rope 64, 32 heads)
     R, L, PS = 16, 4096, 64
     cache = torch.randn(R * L // PS, PS, 576, device=dev, dtype=torch.bfloat16)
@@ -317,6 +335,79 @@ def secondary_lines(dev, peaks, peak_src):
     return out
 
 
+def rank_blocks(world: int, rank: int):
+    """This rank's (batch x kv-head) rectangles of config 2's GQA groups."""
+    from fastest_flash_attention_b200.partition import gqa_group_blocks
+    return gqa_group_blocks(CFG["B"], CFG["Hkv"], rank, world)
+
+
+def block_flops(blocks) -> float:
+    G = CFG["Hq"] // CFG["Hkv"]
+    return sum(fwd_flops(b1 - b0, (h1 - h0) * G, CFG["S"], CFG["D"]) for b0, b1, h0, h1 in blocks)
+
+
+def multi_gpu_lines(dev, world, rank, peaks, peak_src):
+    """Lines only a multi-GPU run has, every rank taking part: config 4 decode
+    split by request (greedy LPT on context length) and the sequence-sharded
+    ring (zigzag, forward and backward) on one long causal sequence.  Times
+    are CUDA events, max over ranks; values are whole-job aggregates."""
+    from fastest_flash_attention_b200 import paged_decode
+    from fastest_flash_attention_b200.partition import lpt_partition
+    from fastest_flash_attention_b200.ring import ring_attention_backward, ring_attention_forward, zigzag_shard
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    out = {}
+    q, kp, vp, bt, lens, tot, mx = paged_decode_inputs(dev)
+    lens_h = lens.cpu().tolist()
+    mine = lpt_partition([float(x) for x in lens_h], world)[rank]
+    idx = torch.tensor(mine, dtype=torch.long, device=dev)
+    q_r, bt_r, lens_r = q[idx].contiguous(), bt[idx].contiguous(), lens[idx].contiguous()
+    mx_r = max(lens_h[i] for i in mine) if mine else 0
+    if mine:
+        fn = lambda: paged_decode(q_r, kp, vp, bt_r, lens_r, max_ctx=mx_r)  # noqa: E731
+        ms_local = _time(fn, 20, dev)
+    else:
+        ms_local = 0.0
+    ms = max_over_ranks(ms_local, world)
+    byts = tot * 8 * 128 * 2 * 2 + q.numel() * 2 * 2
+    out["paged_decode_cfg4_split"] = {
+        "workload": "config 4 (64 req, ctx U[512,32768], page 16, Hq 32/Hkv 8, D 128, bf16) split by request, "
+                    "greedy LPT on context length", "ms": ms, "gbs": byts / ms / 1e6,
+        "frac_of_hbm_per_gpu": byts / ms / 1e6 / hbm / world, "requests_this_rank": len(mine),
+        "ctx_this_rank": int(sum(lens_h[i] for i in mine))}
+    del q, kp, vp, bt, lens, q_r, bt_r, lens_r
+    torch.cuda.empty_cache()
+    # ring: B=1 Hq=32 Hkv=8 D=128, 65536 causal positions, zigzag shards
+    S_tot, Hq, Hkv, D = 65536, 32, 8, 128
+    g = torch.Generator().manual_seed(11)
+    full = [torch.randn(1, h, S_tot, D, generator=g).to(torch.bfloat16) for h in (Hq, Hkv, Hkv, Hq)]
+    qs, ks, vs, dos = (zigzag_shard(t, rank, world).contiguous().to(dev) for t in full)
+    del full
+    sc = 1 / math.sqrt(D)
+    fwd = lambda: ring_attention_forward(qs, ks, vs, scale=sc, causal=True, return_lse=True,  # noqa: E731
+                                         layout="zigzag")
+    o, lse = fwd()
+    bwd = lambda: ring_attention_backward(dos, qs, ks, vs, o, lse, scale=sc, causal=True,  # noqa: E731
+                                          layout="zigzag")
+    res = {}
+    for name, fn in (("fwd", fwd), ("bwd", bwd)):
+        fn()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        res[name] = max_over_ranks(e0.elapsed_time(e1) / 3, world)
+    ff = fwd_flops(1, Hq, S_tot, D)
+    out["ring_cp_zigzag"] = {
+        "workload": f"sequence-sharded ring, B=1 Hq=32 Hkv=8 D=128, {S_tot} causal positions, zigzag over "
+                    f"{world} GPUs (NCCL p2p K/V exchange)", "fwd_ms": res["fwd"], "bwd_ms": res["bwd"],
+        "fwd_tflops": ff / res["fwd"] / 1e9, "bwd_tflops": 2.5 * ff / res["bwd"] / 1e9}
+    return out
+
+
 def run_ours(args, world, rank, local):
     from fastest_flash_attention_b200 import fastest_flash_attn_forward
     from fastest_flash_attention_b200.attention import flash_fwd
@@ -324,15 +415,25 @@ def run_ours(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    G = Hq // Hkv
     scale = 1.0 / math.sqrt(D)
-    q_h, k_h, v_h = make_inputs("cpu", seed=rank)
-    q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
-    flops = fwd_flops(B, Hq, S, D)
+    # Every rank draws the same full batch and keeps its GQA groups: strong
+    # scaling of one fixed config-2 job, no collective on the data path.
+    q_h, k_h, v_h = make_inputs("cpu", seed=0)
+    blocks = rank_blocks(world, rank)
+    parts = [(q_h[b0:b1, h0 * G:h1 * G].contiguous().to(dev), k_h[b0:b1, h0:h1].contiguous().to(dev),
+              v_h[b0:b1, h0:h1].contiguous().to(dev)) for b0, b1, h0, h1 in blocks]
+    flops = fwd_flops(B, Hq, S, D)            # the whole job
+    flops_rank = block_flops(blocks)          # this rank's launches
     stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for q, k, v in parts:
+            flash_fwd(q, k, v, scale=scale, causal=True)
 
     # ---- device-resident timing (value + roofline) ----
     for _ in range(args.warmup):
-        flash_fwd(q, k, v, scale=scale, causal=True)
+        step()
     torch.cuda.synchronize(dev)
     _lib.check_device_errors(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -345,7 +446,7 @@ def run_ours(args, world, rank, local):
         t0.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
-            flash_fwd(q, k, v, scale=scale, causal=True)
+            step()
             ends[i].record(stream)
         t1.record(stream)
         torch.cuda.synchronize(dev)
@@ -354,7 +455,7 @@ def run_ours(args, world, rank, local):
     ms_local = t0.elapsed_time(t1) / args.steps
     launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
     ms = max_over_ranks(ms_local, world)
-    value = world * flops / (ms * 1e-3) / 1e12
+    value = flops / (ms * 1e-3) / 1e12
 
     if args.kernel_only:
         if rank == 0:
@@ -366,42 +467,42 @@ def run_ours(args, world, rank, local):
     qp, kp, vp = q_h.pin_memory(), k_h.pin_memory(), v_h.pin_memory()
     o_host = torch.empty(q_h.shape, dtype=torch.bfloat16).pin_memory()
     lse_host = torch.empty((B, Hq, S, 1), dtype=torch.float32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (qp, kp, vp))
-    d2h = o_host.numel() * 2 + lse_host.numel() * 4
 
     # Chunks of one batch element and half its kv heads (each kv head with its
-    # group of query heads: complete GQA attention problems) on three streams:
-    # the H2D copy of chunk c+1 and the D2H copy of chunk c-1 overlap the
-    # forward of chunk c, so the step costs about the PCIe time of the inputs
-    # plus one chunk.  (Smaller chunks were measured slower: the host-side call
-    # overhead then no longer hides behind the copies.)  Device input buffers
-    # are allocated once, outside the timed region; every byte of input and
-    # output still crosses PCIe inside it.
+    # group of query heads: complete GQA attention problems), restricted to
+    # this rank's groups, on three streams: the H2D copy of chunk c+1 and the
+    # D2H copy of chunk c-1 overlap the forward of chunk c, so the step costs
+    # about the PCIe time of the inputs plus one chunk.  (Smaller chunks were
+    # measured slower: the host-side call overhead then no longer hides behind
+    # the copies.)  Device input buffers are allocated once, outside the timed
+    # region; every byte of input and output still crosses PCIe inside it.
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     q_d, k_d, v_d = (torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (qp, kp, vp))
-    G = Hq // Hkv
     KV_CHUNK = max(1, Hkv // 2)
+    chunks = [(b, g0, min(g0 + KV_CHUNK, h1)) for b0, b1, h0, h1 in blocks for b in range(b0, b1)
+              for g0 in range(h0, h1, KV_CHUNK)]
+    h2d = sum((qp[b, g0 * G:g1 * G].numel() + 2 * kp[b, g0:g1].numel()) * 2 for b, g0, g1 in chunks)
+    d2h = sum(o_host[b, g0 * G:g1 * G].numel() * 2 + lse_host[b, g0 * G:g1 * G].numel() * 4 for b, g0, g1 in chunks)
 
     def e2e_step():
         s_h2d.wait_stream(stream)
         s_d2h.wait_stream(stream)
-        for b in range(B):
-            for g0 in range(0, Hkv, KV_CHUNK):
-                hk = slice(g0, g0 + KV_CHUNK)
-                hq = slice(g0 * G, (g0 + KV_CHUNK) * G)
-                with torch.cuda.stream(s_h2d):
-                    q_d[b, hq].copy_(qp[b, hq], non_blocking=True)
-                    k_d[b, hk].copy_(kp[b, hk], non_blocking=True)
-                    v_d[b, hk].copy_(vp[b, hk], non_blocking=True)
-                stream.wait_stream(s_h2d)
-                o, lse = fastest_flash_attn_forward(q_d[b:b + 1, hq], k_d[b:b + 1, hk], v_d[b:b + 1, hk],
-                                                    causal=True, return_lse=True)
-                s_d2h.wait_stream(stream)
-                with torch.cuda.stream(s_d2h):
-                    o.record_stream(s_d2h)
-                    lse.record_stream(s_d2h)
-                    o_host[b, hq].copy_(o[0], non_blocking=True)
-                    lse_host[b, hq].copy_(lse[0], non_blocking=True)
+        for b, g0, g1 in chunks:
+            hk = slice(g0, g1)
+            hq = slice(g0 * G, g1 * G)
+            with torch.cuda.stream(s_h2d):
+                q_d[b, hq].copy_(qp[b, hq], non_blocking=True)
+                k_d[b, hk].copy_(kp[b, hk], non_blocking=True)
+                v_d[b, hk].copy_(vp[b, hk], non_blocking=True)
+            stream.wait_stream(s_h2d)
+            o, lse = fastest_flash_attn_forward(q_d[b:b + 1, hq], k_d[b:b + 1, hk], v_d[b:b + 1, hk],
+                                                causal=True, return_lse=True)
+            s_d2h.wait_stream(stream)
+            with torch.cuda.stream(s_d2h):
+                o.record_stream(s_d2h)
+                lse.record_stream(s_d2h)
+                o_host[b, hq].copy_(o[0], non_blocking=True)
+                lse_host[b, hq].copy_(lse[0], non_blocking=True)
         stream.wait_stream(s_d2h)
 
     e2e_steps = max(3, min(args.steps, 10))
@@ -417,36 +518,42 @@ def run_ours(args, world, rank, local):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
-    e2e_val = world * flops / (e2e_ms * 1e-3) / 1e12
+    e2e_val = flops / (e2e_ms * 1e-3) / 1e12
     _lib.check_device_errors(dev)
 
+    peaks, peak_src = load_peaks()
+    del parts, q_d, k_d, v_d
+    torch.cuda.empty_cache()
+    multi = multi_gpu_lines(dev, world, rank, peaks, peak_src) if world > 1 and not args.no_secondary else None
     if rank != 0:
         return
-    peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    achieved = flops / (launch_ms * 1e-3) / 1e12
+    achieved = flops_rank / (launch_ms * 1e-3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "fwd_gqa_prefill_traffic.json"
-    if tf.exists():
+    if tf.exists() and world == 1:
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*D^-1/4)",
         "config": workload_config(world),
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms, "api": "fastest_flash_attn_forward(causal=True, return_lse=True) per (batch element, half its kv heads with their query-head groups); H2D, forward and D2H pipelined on three streams"},
-        "gpu_launches": args.steps,
+                "ms_per_step": e2e_ms, "bytes_are": "rank 0's copies (every rank moves its own groups' share)",
+                "api": "fastest_flash_attn_forward(causal=True, return_lse=True) per (batch element, half its kv "
+                       "heads with their query-head groups); H2D, forward and D2H pipelined on three streams"},
+        "gpu_launches": args.steps * len(blocks),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_src} bf16_tflops (burst)", "kernel": "ffa_fwd_kernel<bf16,128>",
-                     "algorithmic_flops_per_launch": flops},
+                     "algorithmic_flops_per_launch": flops_rank / max(1, len(blocks)),
+                     "note": "rank 0's launches"},
         "clocks": clk.summary(),
     }
     if not args.no_secondary:
-        del q, k, v
-        torch.cuda.empty_cache()
         line["secondary"] = secondary_lines(dev, peaks, peak_src)
+        if multi:
+            line["secondary"].update(multi)
     if world == 1:
         runs = [cpu_reference_sample(q_h, k_h, v_h) for _ in range(3)]
         tfc = statistics.median(r[0] for r in runs)

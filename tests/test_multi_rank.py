@@ -3,9 +3,9 @@ would launch them (RANK / WORLD_SIZE / LOCAL_RANK / MASTER_* from the
 environment, rendezvous on 127.0.0.1).
 
 Checked: the process group comes up, the timed value is the max over ranks,
-barriers pass, every rank draws its own independent shard of inputs (weak
-scaling by batch, no collective on the data path), and only rank 0 runs the
-CPU reference arm.
+barriers pass, every rank draws the same seeded job and keeps a disjoint
+share of its GQA groups (strong scaling, no collective on the data path),
+and only rank 0 runs the CPU reference arm.
 """
 import os
 import socket
@@ -35,8 +35,9 @@ def _worker(rank: int, world: int, port: int, out):
     assert dist.get_backend() == "gloo"
     bench.barrier(w)
     ms = bench.max_over_ranks(1.5 + rank, w)
-    q, _, _ = bench.make_inputs("cpu", seed=rank)
+    q, _, _ = bench.make_inputs("cpu", seed=0)
     digest = float(q[0, 0, :64].float().sum())
+    blocks = bench.rank_blocks(w, r)
 
     class Args:
         gpus, steps, warmup = world, 1, 0
@@ -45,7 +46,7 @@ def _worker(rank: int, world: int, port: int, out):
     if rank != 0:
         ran = bench.run_reference(Args, w, r)
     bench.barrier(w)
-    out.put((rank, ms, digest, ran))
+    out.put((rank, ms, digest, ran, blocks, bench.block_flops(blocks)))
     dist.destroy_process_group()
 
 
@@ -62,5 +63,7 @@ def test_two_gloo_ranks():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert [r[1] for r in res] == [2.5, 2.5]  # max over ranks, seen by every rank
-    assert res[0][2] != res[1][2]             # independent shards per rank
+    assert res[0][2] == res[1][2]             # the same job on every rank
     assert res[1][3] is None                  # rank 1 does not run the CPU arm
+    assert res[0][4] == [(0, 2, 0, 8)] and res[1][4] == [(2, 4, 0, 8)]  # batch halves
+    assert res[0][5] == res[1][5]             # equal work
