@@ -31,6 +31,8 @@ STATUS_NAMES = {
 }
 
 DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1}
+# activation / weight dtypes the MLA projection entry points also accept
+IN_DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 _c_void_p = ctypes.c_void_p
 _c_int = ctypes.c_int
@@ -62,6 +64,15 @@ SIGNATURES: dict[str, tuple] = {
         _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
         _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
     ]),
+    "ffa_bwd_masked": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # dout q k v o lse
+        _c_void_p, _c_void_p, _c_void_p,  # dq dk dv
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,  # dtype B Hq Hkv Sq Skv D Dv
+        _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p,  # strides q k v o do dq dk dv
+        _c_float, _c_int, _c_int, _c_int, _c_float,  # scale causal q_offset window softcap
+        _c_void_p, _c_int, _c_int, _c_int, _c_int,  # block_mask n_br n_bc bq bkv
+        _c_void_p, _c_size_t, _c_u32p, _c_void_p,  # workspace bytes err stream
+    ]),
     "ffa_bwd_noalloc": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # dout q k v o lse
         _c_void_p, _c_void_p, _c_void_p,  # dq dk dv
@@ -89,6 +100,20 @@ SIGNATURES: dict[str, tuple] = {
     "ffa_merge_partial": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # o_acc lse_acc o_part lse_part
         _c_int, ctypes.c_int64, _c_int, _c_void_p,  # dtype rows D stream
+    ]),
+    "ffa_mla_q_absorb": (_c_int, [
+        _c_void_p, _c_i64p, _c_void_p, _c_i64p, _c_void_p, _c_i64p,  # q_nope s q_rope s w_uk s
+        _c_void_p, _c_void_p, _c_void_p, _c_i64p,  # pos inv_freq out s
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,  # in lat R H d L rope stream
+    ]),
+    "ffa_mla_o_absorb": (_c_int, [
+        _c_void_p, _c_i64p, _c_void_p, _c_i64p, _c_void_p, ctypes.c_int64,  # o_lat s w_uv s out row_stride
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,  # in lat R H d L rope stream
+    ]),
+    "ffa_mla_latent_append": (_c_int, [
+        _c_void_p, ctypes.c_int64, _c_void_p, ctypes.c_int64,  # lat s kr s
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_int64,  # pos slots inv_freq rows n_slots
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p,  # in lat n L rope stream
     ]),
     "ffa_paged_append": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,  # k_new v_new k_pages v_pages slots

@@ -205,10 +205,13 @@ def fastest_flash_attn_forward(
 def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
               lse: torch.Tensor, *, scale: float, causal: bool = False, q_offset: int = 0,
               window: Optional[int] = None, softcap: Optional[float] = None,
+              block_mask: Optional[torch.Tensor] = None, mask_block: Tuple[int, int] = (64, 64),
               compute_dtype: Optional[torch.dtype] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Run the deterministic sm_100a backward on 4-D tensors.
 
     lse: [B, Hq, Sq] (or [B, Hq, Sq, 1]) natural-log LSE from the forward.
+    block_mask / mask_block: the tile mask the forward was given (masked
+    pairs contribute nothing to any gradient).
     Returns (dq, dk, dv) in the kernel dtype; dk/dv have k's head count
     (GQA groups are summed inside the kernel).
     """
@@ -228,7 +231,8 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
         kd, kv = kdims
         dq, dk, dv = flash_bwd(_pad_last(dout.to(dt), kv), _pad_last(q.to(dt), kd), _pad_last(k.to(dt), kd),
                                _pad_last(v.to(dt), kv), _pad_last(o.to(dt), kv), lse, scale=scale, causal=causal,
-                               q_offset=q_offset, window=window, softcap=softcap, compute_dtype=compute_dtype)
+                               q_offset=q_offset, window=window, softcap=softcap, block_mask=block_mask,
+                               mask_block=mask_block, compute_dtype=compute_dtype)
         return dq[..., :D], dk[..., :D], dv[..., :Dv]
     q, k, v, o, dout = (_tma_ready(t, dt) for t in (q, k, v, o, dout))
     if lse.dim() == 4:
@@ -240,14 +244,20 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     lib = _lib.load()
     ws_bytes = lib.ffa_bwd_workspace_size(B, Hq, Sq)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    common = (dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+              dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, v.shape[3],
+              _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o), _strides_bhs(dout),
+              _strides_bhs(dq), _strides_bhs(dk), _strides_bhs(dv),
+              float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0))
+    tail = (ws.data_ptr(), ws_bytes, _lib.err_word(q.device).data_ptr(), _lib.stream_of(q))
     with torch.cuda.device(q.device):
-        st = lib.ffa_bwd(
-            dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, v.shape[3],
-            _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o), _strides_bhs(dout),
-            _strides_bhs(dq), _strides_bhs(dk), _strides_bhs(dv),
-            float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),
-            ws.data_ptr(), ws_bytes, _lib.err_word(q.device).data_ptr(), _lib.stream_of(q))
+        if block_mask is None:
+            st = lib.ffa_bwd(*common, *tail)
+        else:
+            bm = block_mask.to(device=q.device, dtype=torch.uint8).contiguous()
+            st = lib.ffa_bwd_masked(*common, bm.data_ptr(), bm.shape[0], bm.shape[1], int(mask_block[0]),
+                                    int(mask_block[1]), *tail)
+            bm.record_stream(torch.cuda.current_stream(q.device))
     _lib.check(st, "ffa_bwd")
     if _lib.sync_check_enabled():
         _lib.check_device_errors(q.device)
@@ -268,16 +278,21 @@ def fastest_flash_attn_backward(
     softcap: Optional[float] = None,
     sliding_window: Optional[int] = None,
     q_offset: int = 0,
+    block_mask: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Backward (ops/attention_backward.py:19-76): (dq, dk, dv) from the
     forward's output and LSE, recomputing the attention tile by tile.
 
-    ``block_size`` is accepted for compatibility (tiles are fixed at 128).
-    Gradients come back in the dtypes of q, k and v.
+    ``block_size`` sets the granularity of ``block_mask`` (as in the forward);
+    the kernel's own tiles are fixed.  ``block_mask`` goes beyond the
+    reference, whose backward ignores it: given the forward's mask, the
+    gradients are those of the masked forward.  Gradients come back in the
+    dtypes of q, k and v.
     """
+    bs = block_size if block_size is not None else auto_select_block_size(q.shape[-2], k.shape[-2], q.shape[-1])
     dq, dk, dv = flash_bwd(grad_output, q, k, v, output, lse, scale=scale if scale is not None else
                            1.0 / math.sqrt(q.shape[-1]), causal=causal, q_offset=q_offset, window=sliding_window,
-                           softcap=softcap)
+                           softcap=softcap, block_mask=block_mask, mask_block=(bs, bs))
     return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
 
 
@@ -287,11 +302,12 @@ class FastestFlashAttnFunc(Function):
     Accepts GQA (fewer K/V heads than query heads) natively."""
 
     @staticmethod
-    def forward(ctx, q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass):
+    def forward(ctx, q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass, block_mask=None):
         output, lse = fastest_flash_attn_forward(
             q, k, v, scale=scale, causal=causal, block_size=block_size, softcap=softcap,
-            sliding_window=sliding_window, two_pass=two_pass, return_lse=True)
+            sliding_window=sliding_window, two_pass=two_pass, block_mask=block_mask, return_lse=True)
         ctx.save_for_backward(q, k, v, output, lse)
+        ctx.block_mask = block_mask
         ctx.scale = scale
         ctx.causal = causal
         ctx.block_size = block_size
@@ -307,10 +323,10 @@ class FastestFlashAttnFunc(Function):
             q, k, v, output, lse, grad_output = (t.unsqueeze(1) for t in (q, k, v, output, lse, grad_output))
         dq, dk, dv = fastest_flash_attn_backward(
             grad_output, q, k, v, output, lse, scale=ctx.scale, causal=ctx.causal, block_size=ctx.block_size,
-            softcap=ctx.softcap, sliding_window=ctx.sliding_window)
+            softcap=ctx.softcap, sliding_window=ctx.sliding_window, block_mask=ctx.block_mask)
         if was_3d:
             dq, dk, dv = dq.squeeze(1), dk.squeeze(1), dv.squeeze(1)
-        return dq, dk, dv, None, None, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None, None, None
 
 
 def fastest_flash_attn_func(
@@ -323,6 +339,10 @@ def fastest_flash_attn_func(
     softcap: Optional[float] = None,
     sliding_window: Optional[int] = None,
     two_pass: bool = False,
+    block_mask: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """Differentiable attention (ops/attention_func.py:93-125)."""
-    return FastestFlashAttnFunc.apply(q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass)
+    """Differentiable attention (ops/attention_func.py:93-125).  The trailing
+    ``block_mask`` (tiles of ``block_size``) is an addition: the reference's
+    autograd path has no block mask."""
+    return FastestFlashAttnFunc.apply(q, k, v, scale, causal, block_size, softcap, sliding_window, two_pass,
+                                      block_mask)

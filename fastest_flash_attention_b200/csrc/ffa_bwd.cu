@@ -64,6 +64,10 @@ struct BwdParams {
   float sc_small;      // |raw score| below which tanh_small is accurate (0.5 / sc_pre)
   int use_softcap;
   int causal, window;
+  // optional tile mask [n_br, n_bc] of (mask_bq x mask_bkv) blocks, the one
+  // the forward was given: masked pairs get P = 0 (nullptr: none)
+  const uint8_t* block_mask;
+  int n_br, n_bc, mask_bq, mask_bkv;
   ErrCtx ec;
 };
 
@@ -107,19 +111,40 @@ __device__ __forceinline__ void k_range_for_q_tile(const BwdParams& p, int i, in
   }
 }
 
+// Bits of the 32 columns [0, 32) that fall inside [lo, hi] (columns are
+// relative to the unit's first column).
+__device__ __forceinline__ uint32_t range_bits32(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 31);
+  return hi >= lo ? ((2u << (hi - lo)) - 1u) << lo : 0u;
+}
+
+// Block-mask keep bits of 32 consecutive positions [x0, x0 + 32) along one
+// mask axis (blocks of `bs`, `nb` of them), the other axis fixed: `cell(i)`
+// is the mask byte of block i.  Positions past the mask's end are kept (the
+// range test already drops them).
+template <typename Cell>
+__device__ __forceinline__ uint32_t block_mask_bits32(int x0, int bs, int nb, Cell cell) {
+  uint32_t bits = ~0u;
+#pragma unroll 1
+  for (int i = max(x0, 0) / bs; i * bs < x0 + 32 && i < nb; ++i)
+    if (!cell(i)) bits &= ~range_bits32(i * bs - x0, (i + 1) * bs - 1 - x0);
+  return bits;
+}
+
 // P and dS for 16 columns of one TMEM row.  s: raw Q.K scores, dp: dO.V
 // values.  Minus the base-2 LSE and Delta of each column come from smem
 // (COL_STATS, dK/dV kernel: cnl2 / cdl, 16-byte aligned) or are the row's
-// (rnl2 / rdl, dQ kernel).  With MASKED, columns c with (uint)(c - lo) >= cnt
-// are dropped.  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
+// (rnl2 / rdl, dQ kernel).  With MASKED, columns c whose bit c of `keep` is
+// clear are dropped (P = dS = 0).  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
 // pipe); 2: softcap with tanh through ex2 / rcp.  Columns are processed in
 // pairs with packed fp32x2 instructions (per lane the same IEEE operations as
 // the scalar forms: dp - dl is computed as dp + dl * -1, and
 // (dp - dl)(1 - th^2) as (dl - dp)(th^2 - 1), both exact rewrites).
 template <typename T, bool WRITE_P, bool COL_STATS, int MODE, bool MASKED>
 __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
-                                            const float* cnl2, const float* cdl, float rnl2, float rdl, int lo,
-                                            uint32_t cnt, uint32_t* pk_p, uint32_t* pk_ds) {
+                                            const float* cnl2, const float* cdl, float rnl2, float rdl,
+                                            uint32_t keep, uint32_t* pk_p, uint32_t* pk_ds) {
 #pragma unroll
   for (int c4 = 0; c4 < 16; c4 += 4) {
     float2 nl2[2], dl[2];
@@ -154,8 +179,8 @@ __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* 
       }
       float2 pr = make_float2(ex2(x.x), ex2(x.y));
       if (MASKED) {
-        pr.x = ((uint32_t)(c - lo) < cnt) ? pr.x : 0.f;
-        pr.y = ((uint32_t)(c + 1 - lo) < cnt) ? pr.y : 0.f;
+        pr.x = ((keep >> c) & 1u) ? pr.x : 0.f;
+        pr.y = ((keep >> (c + 1)) & 1u) ? pr.y : 0.f;
       }
       const float2 dv = fmul2(pr, g);
       if (WRITE_P) pk_p[c / 2] = pack2<T>(pr.x, pr.y);
@@ -167,9 +192,9 @@ __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* 
 template <typename T, bool WRITE_P, bool COL_STATS, bool MASKED>
 __device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
                                                  const float* cnl2, const float* cdl, float rnl2, float rdl,
-                                                 int lo, uint32_t cnt, uint32_t* pk_p, uint32_t* pk_ds) {
+                                                 uint32_t keep, uint32_t* pk_p, uint32_t* pk_ds) {
   if (!p.use_softcap) {
-    bwd_chunk16<T, WRITE_P, COL_STATS, 0, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 0, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
     return;
   }
   // The cap is usually far above the scores, so tanh's argument is small:
@@ -178,9 +203,9 @@ __device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint3
 #pragma unroll
   for (int c = 0; c < 16; c += 2) mx = fmax3(mx, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
   if (__all_sync(0xffffffffu, mx <= p.sc_small))
-    bwd_chunk16<T, WRITE_P, COL_STATS, 1, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 1, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
   else
-    bwd_chunk16<T, WRITE_P, COL_STATS, 2, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 2, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
 }
 
 // Stores 16-byte chunk `chunk` of row `row` of a 128-byte-swizzled K-major
@@ -198,16 +223,16 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, uint
 // (Releasing S before dP is read was measured slower: the two loads then
 // no longer overlap.)
 // Column statistics come from smem (COL_STATS: cnl2 / cdl for the first
-// column) or are the row's (rnl2, rdl).  The row keeps columns
-// [keep_lo, keep_hi] of the 32; `masked` (warp-uniform) is false when no row
-// of the warp drops any column.  Before storing, waits (if pt_parity >= 0)
+// column) or are the row's (rnl2, rdl).  The row keeps the columns whose bit
+// is set in `keep` (bit c = column c of the 32); `masked` (warp-uniform) is
+// false when no row of the warp drops any column.  Before storing, waits (if pt_parity >= 0)
 // for `pt_free` to show that the smem tiles' previous contents were consumed;
 // then P^T (WRITE_P) goes to sP and dS to sDS, as 16-byte chunks
 // 4*half .. 4*half+3 of the row.  Returns false if that wait gave up.
 template <typename T, bool WRITE_P, bool COL_STATS>
 __device__ __forceinline__ bool bwd_unit(const BwdParams& p, uint32_t tS, uint32_t tDP, uint64_t* tmem_free,
-                                         const float* cnl2, const float* cdl, float rnl2, float rdl, int keep_lo,
-                                         int keep_hi, bool masked, uint64_t* pt_free, int pt_parity,
+                                         const float* cnl2, const float* cdl, float rnl2, float rdl,
+                                         uint32_t keep, bool masked, uint64_t* pt_free, int pt_parity,
                                          volatile int* abort_flag, uint8_t* sP, uint8_t* sDS, int row, int half) {
   uint32_t s[32], d[32];
   tmem_ld32(tS, s);
@@ -223,13 +248,10 @@ __device__ __forceinline__ bool bwd_unit(const BwdParams& p, uint32_t tS, uint32
     const float* n2 = COL_STATS ? cnl2 + 16 * k : nullptr;
     const float* d2 = COL_STATS ? cdl + 16 * k : nullptr;
     if (masked) {
-      const int lo = max(keep_lo - 16 * k, 0);
-      const int z = min(keep_hi - 16 * k, 15);
-      const uint32_t cnt = z >= lo ? (uint32_t)(z - lo + 1) : 0u;
-      bwd_chunk16_mode<T, WRITE_P, COL_STATS, true>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, lo, cnt,
-                                                    pp + 8 * k, pd + 8 * k);
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, true>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl,
+                                                    (keep >> (16 * k)) & 0xffffu, pp + 8 * k, pd + 8 * k);
     } else {
-      bwd_chunk16_mode<T, WRITE_P, COL_STATS, false>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, 0, 16u,
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, false>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, 0xffffu,
                                                      pp + 8 * k, pd + 8 * k);
     }
   }
@@ -702,12 +724,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_after();
       const int s = u % NS;
       const int q0 = (i_lo + u % n_i) * BWD_BS + 32 * half;
-      const int keep_lo = q_keep_lo - q0, keep_hi = q_keep_hi - q0;
-      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31);
+      uint32_t keep = range_bits32(q_keep_lo - q0, q_keep_hi - q0);
+      if (p.block_mask != nullptr && key < p.Skv) {  // queries are the mask's rows here
+        const uint8_t* mcol = p.block_mask + key / p.mask_bkv;
+        keep &= block_mask_bits32(q0, p.mask_bq, p.n_br, [&](int br) { return mcol[(size_t)br * p.n_bc] != 0; });
+      }
+      const bool masked = !__all_sync(0xffffffffu, keep == ~0u);
       const float* nl2 = sStat + 2 * BWD_BS * s + 32 * half;
       // this pair's P^T / dS^T smem tiles are free once unit u-2's accumulation MMAs are done
-      ok = bwd_unit<T, true, true>(p, tS, tDP, &bars->tmem_free[pair], nl2, nl2 + BWD_BS, 0.f, 0.f, keep_lo,
-                                   keep_hi, masked, &bars->pt_free[pair], u >= 2 ? ((u - 2) >> 1) & 1 : -1,
+      ok = bwd_unit<T, true, true>(p, tS, tDP, &bars->tmem_free[pair], nl2, nl2 + BWD_BS, 0.f, 0.f, keep,
+                                   masked, &bars->pt_free[pair], u >= 2 ? ((u - 2) >> 1) & 1 : -1,
                                    abort_flag, sPT + pair * Cfg::PT, sPT + (2 + pair) * Cfg::PT, r, half);
       if (lane == 0) mbar_arrive(&bars->ds_ready[pair]);
     }
@@ -975,10 +1001,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       const int c0 = (j_lo + u) * UK + colw;
-      const int keep_lo = k_keep_lo - c0, keep_hi = k_keep_hi - c0;
-      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31);
+      uint32_t keep = range_bits32(k_keep_lo - c0, k_keep_hi - c0);
+      if (p.block_mask != nullptr) {  // keys are the mask's columns here
+        const uint8_t* mrow = p.block_mask + (size_t)(min(row, p.Sq - 1) / p.mask_bq) * p.n_bc;
+        keep &= block_mask_bits32(c0, p.mask_bkv, p.n_bc, [&](int bc) { return mrow[bc] != 0; });
+      }
+      const bool masked = !__all_sync(0xffffffffu, keep == ~0u);
       ok = bwd_unit<T, false, false>(p, tS, tDP, &bars->tmem_free[bb], nullptr, nullptr, row_nl2, row_dl,
-                                     keep_lo, keep_hi, masked, &bars->pt_free[bb],
+                                     keep, masked, &bars->pt_free[bb],
                                      u >= 2 ? ((u - 2) >> 1) & 1 : -1, abort_flag, nullptr, sDSw + bb * Cfg::DS, r,
                                      chunk_half);
       if (lane == 0) mbar_arrive(&bars->ds_ready[bb]);
@@ -1068,15 +1098,19 @@ extern "C" size_t ffa_bwd_workspace_size(int B, int Hq, int Sq) {
   return 2 * (size_t)B * Hq * sq_pad * sizeof(float) + 256;
 }
 
-extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o,
-                       const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq,
-                       int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
-                       const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
-                       const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
-                       float scale, int causal, int q_offset, int window, float softcap, void* workspace,
-                       size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                              const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv,
+                              int Sq, int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                              const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                              float scale, int causal, int q_offset, int window, float softcap,
+                              const uint8_t* block_mask, int n_br, int n_bc, int mask_bq, int mask_bkv,
+                              void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream) {
   using namespace ffa;
   if (!dout || !q || !k || !v || !o || !lse || !dq || !dk || !dv) return FFA_ERR_INVALID_ARG;
+  if (block_mask && (n_br <= 0 || n_bc <= 0 || mask_bq <= 0 || mask_bkv <= 0 ||
+                     (int64_t)n_br * mask_bq < Sq || (int64_t)n_bc * mask_bkv < Skv))
+    return FFA_ERR_INVALID_ARG;
   if (!q_strides || !k_strides || !v_strides || !o_strides || !do_strides || !dq_strides || !dk_strides ||
       !dv_strides)
     return FFA_ERR_INVALID_ARG;
@@ -1125,6 +1159,11 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
   p.sc_small = p.use_softcap ? 0.5f * softcap / scale : 0.f;
   p.causal = causal;
   p.window = window > 0 ? window : 0;
+  p.block_mask = block_mask;
+  p.n_br = n_br;
+  p.n_bc = n_bc;
+  p.mask_bq = mask_bq;
+  p.mask_bkv = mask_bkv;
   p.ec.err = dev_err;
   p.ec.limit_ns = wait_limit_ns();
 
@@ -1153,4 +1192,16 @@ extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const voi
   if (D == 64) return launch_bwd<__half, 64, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
   if (D == 128) return launch_bwd<__half, 128, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
   return launch_bwd<__half, 192, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+}
+
+extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                       const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq,
+                       int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                       const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                       const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                       float scale, int causal, int q_offset, int window, float softcap, void* workspace,
+                       size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  return ffa_bwd_masked(dout, q, k, v, o, lse, dq, dk, dv, dtype, B, Hq, Hkv, Sq, Skv, D, Dv, q_strides, k_strides,
+                        v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, scale, causal, q_offset,
+                        window, softcap, nullptr, 0, 0, 0, 0, workspace, workspace_bytes, dev_err, stream);
 }

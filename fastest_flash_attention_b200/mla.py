@@ -140,36 +140,94 @@ class MLADecoder:
         self.cache = MLALatentCache(max_pages, page_size, mla.latent_dim, mla.rope_dim, dtype, dev)
         self.dtype = dtype
 
-    def _latent_entries(self, x: torch.Tensor, offset: int) -> torch.Tensor:
-        """[S, latent + rope] cache rows for x [S, hidden] at positions offset..offset+S-1."""
-        lat = self.mla.kv_down_proj(x)
-        kr = self.mla.rope(self.mla.k_rope_proj(x).unsqueeze(0), offset)[0]
-        return torch.cat([lat, kr], dim=-1)
+    def _weights(self):
+        """[q_proj | q_rope_proj | kv_down_proj | k_rope_proj] stacked into one
+        matrix, so the step's four input projections are one GEMM (rebuilt
+        when any of the weights changes)."""
+        m = self.mla
+        ws = (m.q_proj.weight, m.q_rope_proj.weight, m.kv_down_proj.weight, m.k_rope_proj.weight)
+        key = tuple((w.data_ptr(), w._version) for w in ws)
+        if getattr(self, "_w_key", None) != key:
+            self._w_cat = torch.cat([w.detach() for w in ws], dim=0)
+            self._w_key = key
+        return self._w_cat
+
+    def _append_latents(self, lat: torch.Tensor, kr: torch.Tensor, pos: List[int], slots: List[int]) -> None:
+        """Cache rows [lat | rope(kr, pos)] for tokens whose rows are lat [n, L]
+        and kr [n, rope] (last dim contiguous), in one launch."""
+        dev = self.cache.pages.device
+        pos_t = torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True)
+        slot_t = torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True)
+        rows = self.cache.pages.view(-1, self.cache.pages.shape[-1])
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            st = lib.ffa_mla_latent_append(lat.data_ptr(), lat.stride(0), kr.data_ptr(), kr.stride(0),
+                                           pos_t.data_ptr(), slot_t.data_ptr(), self._inv_freq().data_ptr(),
+                                           rows.data_ptr(), rows.shape[0], _lib.IN_DTYPE_CODE[lat.dtype],
+                                           _lib.DTYPE_CODE[rows.dtype], lat.shape[0], lat.shape[1], kr.shape[1],
+                                           _lib.stream_of(rows))
+        _lib.check(st, "ffa_mla_latent_append")
+
+    def _inv_freq(self) -> torch.Tensor:
+        return self.mla.rope.inv_freq.to(torch.float32).contiguous()
 
     @torch.no_grad()
     def prefill(self, x: torch.Tensor, seq_ids: Sequence[int]) -> torch.Tensor:
         """Run the module on x [B, S, hidden] and cache every position's latent."""
+        m = self.mla
+        lat_all = m.kv_down_proj(x)   # [B, S, L]
+        kr_all = m.k_rope_proj(x)     # [B, S, rope]
         for b, sid in enumerate(seq_ids):
-            self.cache.append(sid, self._latent_entries(x[b], self.cache.sequences.get(sid, {"len": 0})["len"]))
+            start = self.cache.sequences.get(sid, {"len": 0})["len"]
+            S = x.shape[1]
+            slots = self.cache._slots(sid, S)
+            self._append_latents(lat_all[b].contiguous(), kr_all[b].contiguous(), list(range(start, start + S)),
+                                 slots)
         return self.mla(x)
 
     @torch.no_grad()
     def step(self, x: torch.Tensor, seq_ids: Sequence[int]) -> torch.Tensor:
-        """One new token per sequence: x [R, 1, hidden] -> [R, 1, hidden]."""
+        """One new token per sequence: x [R, 1, hidden] -> [R, 1, hidden].
+
+        One GEMM for the four input projections, then three launches of this
+        package (latent append with k RoPE; query absorption with q RoPE; the
+        paged latent decode) and one more (value absorption into o_proj's
+        input rows) before the o_proj GEMM.  No per-request Python loop runs
+        on the device path."""
         m = self.mla
         R = x.shape[0]
-        H, d, r = m.num_heads, m.head_dim, m.rope_dim
+        H, d, r, L = m.num_heads, m.head_dim, m.rope_dim, m.latent_dim
         pos = [self.cache.sequences.get(s, {"len": 0})["len"] for s in seq_ids]
-        for i, sid in enumerate(seq_ids):
-            self.cache.append(sid, self._latent_entries(x[i], pos[i]))
-        q_nope = m.q_proj(x[:, 0]).view(R, H, d)
-        q_rope = m.q_rope_proj(x[:, 0]).view(R, H, r)
-        q_rope = torch.stack([m.rope(q_rope[i:i + 1].unsqueeze(2), pos[i])[0, :, 0] for i in range(R)])
+        slots = [self.cache._slots(s, 1)[0] for s in seq_ids]
+        y = x[:, 0] @ self._weights().t()                      # [R, H d + H r + L + r]
+        q_nope = y[:, :H * d].view(R, H, d)
+        q_rope = y[:, H * d:H * (d + r)].view(R, H, r)
+        lat = y[:, H * (d + r):H * (d + r) + L]
+        kr = y[:, H * (d + r) + L:]
+        self._append_latents(lat, kr, pos, slots)
         w_uk, w_uv = absorbed_weights(m)
-        q_lat = torch.einsum("rhd,hdl->rhl", q_nope.float(), w_uk.float())
-        q = torch.cat([q_lat, q_rope.float()], dim=-1).to(self.dtype)
+        lib = _lib.load()
+        dev = x.device
+        pos_t = torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True)
+        q = torch.empty((R, H, L + r), dtype=self.dtype, device=dev)
+        in_code = _lib.IN_DTYPE_CODE[y.dtype]
+        if w_uk.dtype != y.dtype:
+            raise ValueError("MLA decode needs activations and weights of one dtype")
+        with torch.cuda.device(dev):
+            st = lib.ffa_mla_q_absorb(q_nope.data_ptr(), _lib.i64arr(q_nope.stride(0), q_nope.stride(1)),
+                                      q_rope.data_ptr(), _lib.i64arr(q_rope.stride(0), q_rope.stride(1)),
+                                      w_uk.data_ptr(), _lib.i64arr(w_uk.stride(0), w_uk.stride(1)),
+                                      pos_t.data_ptr(), self._inv_freq().data_ptr(), q.data_ptr(),
+                                      _lib.i64arr(q.stride(0), q.stride(1)), in_code, _lib.DTYPE_CODE[self.dtype],
+                                      R, H, d, L, r, _lib.stream_of(q))
+        _lib.check(st, "ffa_mla_q_absorb")
         bt, lens = self.cache.block_table(seq_ids)
         o_lat = mla_decode(q, self.cache.pages, bt, lens, scale=m.scale, max_ctx=max(pos) + 1)
-        o = torch.einsum("rhl,hdl->rhd", o_lat.float(), w_uv.float())
-        o = torch.nn.functional.pad(o, (0, r)).reshape(R, 1, H * (d + r)).to(x.dtype)
-        return m.o_proj(o)
+        o = torch.empty((R, H * (d + r)), dtype=y.dtype, device=dev)
+        with torch.cuda.device(dev):
+            st = lib.ffa_mla_o_absorb(o_lat.data_ptr(), _lib.i64arr(o_lat.stride(0), o_lat.stride(1)),
+                                      w_uv.data_ptr(), _lib.i64arr(w_uv.stride(0), w_uv.stride(1)), o.data_ptr(),
+                                      o.stride(0), in_code, _lib.DTYPE_CODE[o_lat.dtype], R, H, d, L, r,
+                                      _lib.stream_of(o))
+        _lib.check(st, "ffa_mla_o_absorb")
+        return m.o_proj(o).view(R, 1, -1)

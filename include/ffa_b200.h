@@ -42,7 +42,8 @@ typedef enum {
   FFA_ERR_WORKSPACE = 5        /* workspace missing or too small */
 } ffa_status;
 
-typedef enum { FFA_DTYPE_F16 = 0, FFA_DTYPE_BF16 = 1 } ffa_dtype;
+/* F32 is accepted only where an entry point says so (the MLA projections). */
+typedef enum { FFA_DTYPE_F16 = 0, FFA_DTYPE_BF16 = 1, FFA_DTYPE_F32 = 2 } ffa_dtype;
 
 /* Library version (major*10000 + minor*100 + patch). */
 int ffa_version(void);
@@ -103,6 +104,21 @@ int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const
             const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
             const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
             int window, float softcap, void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/* Backward with a block mask: ffa_bwd's arguments plus the forward's tile
+ * mask (block_mask [n_br, n_bc] uint8, blocks of mask_bq queries x mask_bkv
+ * keys, nonzero = kept; the same arguments ffa_fwd takes).  Masked (query,
+ * key) pairs get P = 0, so the gradients are those of the masked forward.
+ * The reference backward (kernels/cpu_reference.py:319-427) ignores the mask;
+ * this defines it as the derivative of its masked forward (:220-224).
+ * ffa_bwd is this call with block_mask = NULL. */
+int ffa_bwd_masked(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+                   void* dq, void* dk, void* dv, int dtype, int B, int Hq, int Hkv, int Sq, int Skv, int D, int Dv,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                   const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+                   const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
+                   int window, float softcap, const uint8_t* block_mask, int n_br, int n_bc, int mask_bq,
+                   int mask_bkv, void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Allocation-free backward.  No counterpart in the reference: this entry
@@ -169,6 +185,41 @@ int ffa_mla_decode(const void* q, const void* ckv_pages, const int* block_table,
                    float* lse, int dtype, int R, int H, int num_pages, int page_size, int max_pages_per_req,
                    const int64_t* q_strides, const int64_t* o_strides, float scale, int chunks_per_split,
                    void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * The projections on either side of the MLA absorbed decode, one launch each.
+ * Replace modules/flash_mla.py:133-152 (q/k RoPE through the RotaryEmbedding
+ * module, kv_up_proj of the whole prefix) for one new token per request:
+ * W_UK / W_UV are the two halves of kv_up_proj.weight viewed [H, 2d, L].
+ * in_dtype (activations, weights, o_absorb output): F32, BF16 or F16;
+ * lat_dtype (decode query, latent output, cache rows): BF16 or F16.
+ * RoPE is half-split with fp32 angles pos * inv_freq[i], i < rope/2.
+ *
+ * ffa_mla_q_absorb: out[r, h, :] = [q_nope[r, h] . W_UK[h] (L) |
+ *   rope(q_rope[r, h], pos[r]) (rope)].  q_nope [R, H, d] strides {r, h};
+ *   q_rope [R, H, rope] strides {r, h}; w_uk [H, d, L] strides {h, j};
+ *   out [R, H, L + rope] strides {r, h}.  L multiple of 64, d <= 192.
+ * ffa_mla_o_absorb: out[r, h (d + rope) + i] = o_lat[r, h] . W_UV[h, i] for
+ *   i < d, and 0 for the rope columns (the reference's zero-padded V):
+ *   o_proj's input rows.  o_lat [R, H, L] strides {r, h}; w_uv [H, d, L]
+ *   strides {h, i}; out rows of stride out_row_stride.  L multiple of 32,
+ *   L <= 1024.
+ * ffa_mla_latent_append: rows[slots[t]] = [lat[t] (L) | rope(kr[t], pos[t])]
+ *   for n_tokens tokens; rows [n_slots, L + rope] contiguous (the latent
+ *   cache's pages viewed as rows); slots outside [0, n_slots) are skipped.
+ * ------------------------------------------------------------------------- */
+int ffa_mla_q_absorb(const void* q_nope, const int64_t* qn_strides, const void* q_rope, const int64_t* qr_strides,
+                     const void* w_uk, const int64_t* w_strides, const int* pos, const float* inv_freq, void* out,
+                     const int64_t* o_strides, int in_dtype, int lat_dtype, int R, int H, int d, int L, int rope,
+                     void* stream);
+
+int ffa_mla_o_absorb(const void* o_lat, const int64_t* ol_strides, const void* w_uv, const int64_t* w_strides,
+                     void* out, int64_t out_row_stride, int in_dtype, int lat_dtype, int R, int H, int d, int L,
+                     int rope, void* stream);
+
+int ffa_mla_latent_append(const void* lat, int64_t lat_row_stride, const void* kr, int64_t kr_row_stride,
+                          const int* pos, const int* slots, const float* inv_freq, void* rows, int64_t n_slots,
+                          int in_dtype, int lat_dtype, int n_tokens, int L, int rope, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Paged-KV append: scatter new K/V tokens into their (page, offset) slots.

@@ -154,3 +154,56 @@ def test_config3_slice_full_length():
     for t, ref, nm in ((qc, rdq, "dq"), (kc, rdk, "dk"), (vc, rdv, "dv")):
         e = rel_err(t.grad, ref)
         assert e <= G_TOL, f"{nm}: rel err {e:.3e}"
+
+
+def _masked_attention_fp32(q, k, v, keep, scale):
+    """Dense fp32 attention with a boolean [Sq, Skv] keep matrix (GQA by repeat)."""
+    g = q.shape[1] // k.shape[1]
+    kr, vr = k.repeat_interleave(g, 1), v.repeat_interleave(g, 1)
+    s = (q @ kr.transpose(-1, -2)) * scale
+    s = s.masked_fill(~keep, float("-inf"))
+    return torch.softmax(s, -1) @ vr
+
+
+@pytest.mark.parametrize("S,Skv,D,bs,causal,window", [
+    (300, 300, 64, 32, False, None),
+    (333, 333, 128, 64, True, None),
+    (256, 200, 64, 16, False, 90),
+])
+def test_backward_with_block_mask(S, Skv, D, bs, causal, window):
+    """Block-sparse training: the gradients of the masked forward (the
+    reference backward ignores block_mask; here it is defined as the
+    derivative of its masked forward, cpu_reference.py:220-224), against fp32
+    autograd through a dense masked attention."""
+    m = ffa()
+    B, Hq, Hkv = 1, 4, 2
+    gen = torch.Generator().manual_seed(31)
+    n_br, n_bc = -(-S // bs), -(-Skv // bs)
+    bm = torch.rand(n_br, n_bc, generator=gen) < 0.6
+    bm[torch.arange(n_br), torch.arange(n_br).clamp(max=n_bc - 1)] = True  # every row keeps a block
+    q, k, v, do = _rand(B, Hq, S, D, seed=41), _rand(B, Hkv, Skv, D, seed=42), _rand(B, Hkv, Skv, D, seed=43), \
+        _rand(B, Hq, S, D, seed=44)
+    qc, kc, vc = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = m.fastest_flash_attn_func(qc, kc, vc, None, causal, bs, None, window, False, bm)
+    o.backward(do.cuda())
+    # fp32 reference
+    qi, ki = torch.arange(S)[:, None], torch.arange(Skv)[None, :]
+    keep = bm.repeat_interleave(bs, 0)[:S].repeat_interleave(bs, 1)[:, :Skv]
+    if causal:
+        keep &= ki <= qi
+    if window:
+        keep &= ki > qi - window
+    assert keep.any(1).all()
+    qf, kf, vf = (t.float().cuda().requires_grad_(True) for t in (q, k, v))
+    of = _masked_attention_fp32(qf, kf, vf, keep.cuda(), 1 / math.sqrt(D))
+    of.backward(do.float().cuda())
+    assert (o.float() - of).abs().max().item() <= 2e-2
+    for t, ref, nm in ((qc, qf, "dq"), (kc, kf, "dk"), (vc, vf, "dv")):
+        e = rel_err(t.grad, ref.grad.cpu().numpy())
+        assert e <= G_TOL, f"{nm}: rel err {e:.3e}"
+    # deterministic with a mask too
+    g1 = [t.grad.clone() for t in (qc, kc, vc)]
+    for t in (qc, kc, vc):
+        t.grad = None
+    m.fastest_flash_attn_func(qc, kc, vc, None, causal, bs, None, window, False, bm).backward(do.cuda())
+    assert all(torch.equal(a, t.grad) for a, t in zip(g1, (qc, kc, vc)))

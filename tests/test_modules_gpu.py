@@ -173,3 +173,67 @@ def test_mla_prefill_config5_full_size_rows():
             err = (y[b, rows].float() - y_ref).abs().max().item() / y_ref.abs().max().item()
             worst = max(worst, err)
     assert worst <= 2e-2, worst
+
+
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
+def test_mla_projection_kernels_vs_torch(wdtype):
+    """The fused projections around the MLA decode (ffa_mla_q_absorb,
+    ffa_mla_o_absorb, ffa_mla_latent_append) against fp32 torch of the same
+    math: q = [q_nope W_UK | rope(q_rope)], o = o_lat W_UV^T with zero rope
+    columns, cache rows [c_kv | rope(k_rope)] (modules/flash_mla.py:133-152)."""
+    from fastest_flash_attention_b200 import _lib
+    from fastest_flash_attention_b200.mla import absorbed_weights
+    m = ffa()
+    torch.manual_seed(7)
+    mod = m.FastestFlashMLA(hidden_size=256, num_heads=32, head_dim=128, latent_dim=512, rope_dim=64).cuda()
+    for prm in mod.parameters():
+        torch.nn.init.normal_(prm, std=0.05)
+    mod = mod.to(wdtype)
+    dec = m.MLADecoder(mod, max_pages=8, page_size=16)
+    R, H, d, r, L = 5, 32, 128, 64, 512
+    pos = [0, 7, 300, 4095, 12345]
+    x = torch.randn(R, 256, device="cuda").to(wdtype)
+    y = x @ dec._weights().t()
+    q_nope, q_rope = y[:, :H * d].view(R, H, d), y[:, H * d:H * (d + r)].view(R, H, r)
+    lat, kr = y[:, H * (d + r):H * (d + r) + L], y[:, H * (d + r) + L:]
+    w_uk, w_uv = absorbed_weights(mod)
+    lib = _lib.load()
+    pos_t = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    inv = mod.rope.inv_freq.float().contiguous()
+    # torch fp32 RoPE with the module's own convention (positions as fp32)
+    ang = torch.tensor(pos, dtype=torch.float32, device="cuda")[:, None] * inv[None, :]
+    cos, sin = ang.cos(), ang.sin()
+
+    def rope(t):  # t [R, ..., r]
+        c = cos.view(R, *([1] * (t.dim() - 2)), r // 2)
+        s_ = sin.view(R, *([1] * (t.dim() - 2)), r // 2)
+        a, b = t[..., :r // 2].float(), t[..., r // 2:].float()
+        return torch.cat([a * c - b * s_, b * c + a * s_], -1)
+
+    q = torch.empty(R, H, L + r, dtype=torch.bfloat16, device="cuda")
+    st = lib.ffa_mla_q_absorb(q_nope.data_ptr(), _lib.i64arr(*q_nope.stride()[:2]), q_rope.data_ptr(),
+                              _lib.i64arr(*q_rope.stride()[:2]), w_uk.data_ptr(), _lib.i64arr(*w_uk.stride()[:2]),
+                              pos_t.data_ptr(), inv.data_ptr(), q.data_ptr(), _lib.i64arr(*q.stride()[:2]),
+                              _lib.IN_DTYPE_CODE[wdtype], _lib.DTYPE_CODE[torch.bfloat16], R, H, d, L, r,
+                              _lib.stream_of(q))
+    _lib.check(st, "ffa_mla_q_absorb")
+    q_ref = torch.cat([torch.einsum("rhd,hdl->rhl", q_nope.float(), w_uk.float()), rope(q_rope)], -1)
+    assert rel(q, q_ref.cpu().numpy()) <= 1e-2
+    o_lat = torch.randn(R, H, L, device="cuda").to(torch.bfloat16)
+    o = torch.full((R, H * (d + r)), 7.0, dtype=wdtype, device="cuda")
+    st = lib.ffa_mla_o_absorb(o_lat.data_ptr(), _lib.i64arr(*o_lat.stride()[:2]), w_uv.data_ptr(),
+                              _lib.i64arr(*w_uv.stride()[:2]), o.data_ptr(), o.stride(0), _lib.IN_DTYPE_CODE[wdtype],
+                              _lib.DTYPE_CODE[torch.bfloat16], R, H, d, L, r, _lib.stream_of(o))
+    _lib.check(st, "ffa_mla_o_absorb")
+    o_ref = torch.nn.functional.pad(torch.einsum("rhl,hdl->rhd", o_lat.float(), w_uv.float()), (0, r))
+    assert rel(o, o_ref.reshape(R, -1).cpu().numpy()) <= 1e-2
+    assert not o.view(R, H, d + r)[..., d:].any()
+    # latent append into scattered slots
+    slots = [3, 17, 40, 41, 127]
+    dec._append_latents(lat, kr, pos, slots)
+    torch.cuda.synchronize()
+    rows = dec.cache.pages.view(-1, L + r)
+    ref_rows = torch.cat([lat.float(), rope(kr)], -1)
+    assert rel(rows[slots], ref_rows.cpu().numpy()) <= 1e-2
+    untouched = [i for i in range(rows.shape[0]) if i not in slots]
+    assert not rows[untouched].any()
