@@ -22,17 +22,43 @@
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
+#include <cstdlib>
+
 namespace ffa {
 
 constexpr int FWD_BM = 128;   // rows per query tile (= TMEM lanes)
-constexpr int FWD_NQT = 2;    // query tiles per CTA
 constexpr int FWD_BN = 128;   // keys per key tile
-constexpr int FWD_THREADS = 384;  // 2 softmax warpgroups + 1 warpgroup for TMA / MMA (2 warps idle)
-// Register budgets after the split: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
-constexpr uint32_t FWD_REGS_SOFTMAX = 208;
-constexpr uint32_t FWD_REGS_OTHER = 88;
-constexpr int FWD_WARP_LOAD = 8;
-constexpr int FWD_WARP_MMA = 9;
+#ifndef FFA_FWD_NQT1_MAX_COLS
+#define FFA_FWD_NQT1_MAX_COLS 2048
+#endif
+constexpr long long FWD_NQT1_MAX_COLS = FFA_FWD_NQT1_MAX_COLS;  // rows this short use one query tile per CTA
+
+// CTA shapes.  NQT = 2 (one CTA per SM): two query tiles whose softmax groups
+// ping-pong inside the CTA.  NQT = 1 (two CTAs per SM, each half the TMEM
+// and under half the shared memory): one query tile per CTA, and the two
+// resident CTAs interleave on the SM's tensor core the way the two groups of
+// an NQT = 2 CTA do, while one CTA's set-up (barriers, TMEM, the first Q / K
+// loads) and epilogue overlap the other's main loop.  That matters when a CTA
+// walks few key tiles (sliding windows, short rows), where set-up and
+// epilogue are a large share of a CTA's time.
+template <int NQT>
+struct FwdShape;
+template <>
+struct FwdShape<2> {
+  static constexpr int THREADS = 384;  // 2 softmax warpgroups + 1 warpgroup for TMA / MMA (2 warps idle)
+  static constexpr int MIN_BLOCKS = 1;
+  // Register budgets after the split: 2 x 128 x 208 + 128 x 88 = 384 x 168 (the launch allocation).
+  static constexpr uint32_t REGS_SOFTMAX = 208, REGS_OTHER = 88;
+  static constexpr int TMEM_COLS = 512;
+};
+template <>
+struct FwdShape<1> {
+  static constexpr int THREADS = 256;  // 1 softmax warpgroup + 1 warpgroup for TMA / MMA (2 warps idle)
+  static constexpr int MIN_BLOCKS = 2;
+  // 128 x 200 + 128 x 56 = 256 x 128 (the launch allocation at two CTAs per SM).
+  static constexpr uint32_t REGS_SOFTMAX = 200, REGS_OTHER = 56;
+  static constexpr int TMEM_COLS = 256;
+};
 constexpr int FWD_MAX_LIST = 2048;  // key tiles recorded per CTA when a block mask filters them
 constexpr float RESCALE_LOG2 = 8.0f;
 #ifndef FFA_FWD_PCH
@@ -43,14 +69,14 @@ constexpr int FWD_PCH = FFA_FWD_PCH;  // P is handed to the MMA warp in FWD_PCH 
 
 // D = query/key head dim, DV = value head dim (DV <= 128; D = 192 with
 // DV = 128 is the MLA prefill shape: 128 "nope" + 64 rotary dims).
-template <int D, int DV>
+template <int D, int DV, int NQT = 2>
 struct FwdCfg {
   static constexpr int TILE = FWD_BM * D * 2;     // one 128-row Q (or K) tile
   static constexpr int VTILE = FWD_BN * DV * 2;   // one 128-row V tile
   static constexpr int BUF = TILE > VTILE ? TILE : VTILE;  // ring slot (holds a K or a V tile)
-  static constexpr int NBUF = (D == 64) ? 8 : (D == 128 ? 4 : 2);
+  static constexpr int NBUF = NQT == 2 ? ((D == 64) ? 8 : (D == 128 ? 4 : 2)) : (D == 64 ? 4 : 2);
   static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = FWD_NQT * TILE;
+  static constexpr int KV_OFF = NQT * TILE;
   static constexpr int BAR_OFF = KV_OFF + NBUF * BUF;
   static constexpr int LIST_OFF = BAR_OFF + 512;
   static constexpr int SMEM = LIST_OFF + FWD_MAX_LIST * 2 + 1024;  // + alignment slack
@@ -98,11 +124,16 @@ enum : uint32_t {
 };
 
 
-template <typename T, int D, int DV>
-__global__ void __launch_bounds__(FWD_THREADS, 1)
+template <typename T, int D, int DV, int NQT>
+__global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLOCKS)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
-  using Cfg = FwdCfg<D, DV>;
+  using Cfg = FwdCfg<D, DV, NQT>;
+  using Shape = FwdShape<NQT>;
+  constexpr int FWD_NQT = NQT;
+  constexpr int FWD_WARP_LOAD = 4 * NQT;     // the warpgroup after the softmax groups
+  constexpr int FWD_WARP_MMA = 4 * NQT + 1;
+  constexpr uint32_t O_COL = NQT * 128;      // TMEM: S_t/P_t at [128 t, ...), O_t at O_COL + 128 t
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
@@ -132,7 +163,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < NQT; ++t) {
       mbar_init(&bars->s_full[t], 1);
       for (int k = 0; k < FWD_PCH; ++k) mbar_init(&bars->p_full[t][k], FWD_BM / 32);  // one arrival per warp
       mbar_init(&bars->o_done[t], 1);
@@ -146,7 +177,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     fence_mbar_init();
   }
   if (warp == FWD_WARP_MMA) {
-    tmem_alloc(&bars->tmem_base, 512);
+    tmem_alloc(&bars->tmem_base, Shape::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == FWD_WARP_LOAD) {
@@ -202,8 +233,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   auto tile_at = [&](int it) -> int { return use_list ? (int)list[it] : j_lo + it; };
   constexpr uint32_t FMT = DtypeFmt<T>::value;
 
-  if (warp >= 8) {
-   regs_dec<FWD_REGS_OTHER>();
+  if (warp >= 4 * NQT) {
+   regs_dec<Shape::REGS_OTHER>();
    if (warp == FWD_WARP_LOAD) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
@@ -270,7 +301,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       // P·V for one chunk of keys (k-steps of 16 keys); chunks are issued as
       // the softmax group releases them.
       auto issue_pv = [&](int t, int buf, bool acc, int chunk) {
-        const uint32_t d = tmem + 256 + t * 128;
+        const uint32_t d = tmem + O_COL + t * 128;
         const uint32_t a = tmem + t * 128;
         const uint64_t vb = v_base + (uint64_t)((buf * Cfg::BUF) >> 4);
         constexpr int KS_PER = FWD_BN / 16 / FWD_PCH;
@@ -285,10 +316,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         ok = mbar_wait_mma(&bars->kv_full[0], 0, p.ec, abort_flag, SITE_FWD_KV_FULL);
         if (ok) {
           tc_fence_after();
-          issue_qk(0, 0);
-          mma_commit(&bars->s_full[0]);
-          issue_qk(1, 0);
-          mma_commit(&bars->s_full[1]);
+          for (int t = 0; t < NQT; ++t) {
+            issue_qk(t, 0);
+            mma_commit(&bars->s_full[t]);
+          }
           mma_commit(&bars->kv_empty[0]);
         }
       }
@@ -329,13 +360,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     __syncwarp();
    }
   } else {
-    regs_inc<FWD_REGS_SOFTMAX>();
+    regs_inc<Shape::REGS_SOFTMAX>();
     // ------------------------------ softmax -------------------------------
     const int t = warp / 4;
     const int r = threadIdx.x % FWD_BM;
     const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
-    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const uint32_t tO = tmem + lane_off + O_COL + t * 128;
     const int row = q_lo + t * FWD_BM + r;
     const int arow = row + p.q_offset;
     float m = -INFINITY, l = 0.f;
@@ -533,19 +564,43 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   __syncthreads();
   if (warp == FWD_WARP_MMA) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, Shape::TMEM_COLS);
   }
 }
 
-template <typename T, int D, int DV>
+template <typename T, int D, int DV, int NQT>
 static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdParams& p,
                       int grid, cudaStream_t stream) {
-  using Cfg = FwdCfg<D, DV>;
-  auto kern = ffa_fwd_kernel<T, D, DV>;
+  using Cfg = FwdCfg<D, DV, NQT>;
+  auto kern = ffa_fwd_kernel<T, D, DV, NQT>;
   static std::atomic<uint64_t> attr_done{0};
   if (int st = smem_attr_once(kern, Cfg::SMEM, attr_done)) return st;
-  kern<<<grid, FWD_THREADS, Cfg::SMEM, stream>>>(mq, mk, mv, p);
+  kern<<<grid, FwdShape<NQT>::THREADS, Cfg::SMEM, stream>>>(mq, mk, mv, p);
   return launch_status();
+}
+
+// Query tiles per CTA.  One tile per CTA (two CTAs per SM) when a CTA would
+// walk few key tiles, so that set-up and epilogue are hidden behind the
+// other resident CTA; two tiles per CTA otherwise.  D = 192 has only the
+// two-tile shape (its tiles do not fit twice in shared memory).
+// FFA_FWD_NQT=1|2 in the environment forces a shape (for measurements).
+static int fwd_query_tiles(int D, int Sq, int Skv, int causal, int window, bool masked) {
+  static const int forced = [] {
+    const char* e = getenv("FFA_FWD_NQT");
+    return e ? atoi(e) : 0;
+  }();
+  if (D == 192) return 2;
+  if (forced == 1 || forced == 2) return forced;
+  // average key columns a query row attends to (upper bound under masks)
+  long long cols = Skv;
+  if (causal) cols = (Skv + 1) / 2 + (Skv > Sq ? Skv - Sq : 0);
+  if (window > 0 && window < cols) cols = window;
+  (void)masked;
+  // Measured (B=8 H=16 S=4096): at D = 64 with a 512-key window one tile per
+  // CTA ran 0.237 ms against 0.296 ms; at D = 128 it was slower in every case
+  // tried (its register budget at two CTAs per SM spills, and its K/V ring
+  // holds only one key tile), so D = 128 keeps two tiles per CTA.
+  return (D == 64 && cols <= FWD_NQT1_MAX_COLS) ? 1 : 2;
 }
 
 }  // namespace ffa
@@ -578,7 +633,8 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   p.Sq = Sq;
   p.Skv = Skv;
   p.q_offset = q_offset;
-  p.n_qblk = (Sq + FWD_BM * FWD_NQT - 1) / (FWD_BM * FWD_NQT);
+  const int nqt = fwd_query_tiles(D, Sq, Skv, causal, window, block_mask != nullptr);
+  p.n_qblk = (Sq + FWD_BM * nqt - 1) / (FWD_BM * nqt);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.use_softcap = softcap > 0.f;
   p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
@@ -611,11 +667,19 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   if (grid > 0x7fffffffLL) return FFA_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FFA_DTYPE_BF16) {
-    if (D == 64) return launch_fwd<__nv_bfloat16, 64, 64>(mq, mk, mv, p, (int)grid, s);
-    if (D == 128) return launch_fwd<__nv_bfloat16, 128, 128>(mq, mk, mv, p, (int)grid, s);
-    return launch_fwd<__nv_bfloat16, 192, 128>(mq, mk, mv, p, (int)grid, s);
+    if (D == 64)
+      return nqt == 1 ? launch_fwd<__nv_bfloat16, 64, 64, 1>(mq, mk, mv, p, (int)grid, s)
+                      : launch_fwd<__nv_bfloat16, 64, 64, 2>(mq, mk, mv, p, (int)grid, s);
+    if (D == 128)
+      return nqt == 1 ? launch_fwd<__nv_bfloat16, 128, 128, 1>(mq, mk, mv, p, (int)grid, s)
+                      : launch_fwd<__nv_bfloat16, 128, 128, 2>(mq, mk, mv, p, (int)grid, s);
+    return launch_fwd<__nv_bfloat16, 192, 128, 2>(mq, mk, mv, p, (int)grid, s);
   }
-  if (D == 64) return launch_fwd<__half, 64, 64>(mq, mk, mv, p, (int)grid, s);
-  if (D == 128) return launch_fwd<__half, 128, 128>(mq, mk, mv, p, (int)grid, s);
-  return launch_fwd<__half, 192, 128>(mq, mk, mv, p, (int)grid, s);
+  if (D == 64)
+    return nqt == 1 ? launch_fwd<__half, 64, 64, 1>(mq, mk, mv, p, (int)grid, s)
+                    : launch_fwd<__half, 64, 64, 2>(mq, mk, mv, p, (int)grid, s);
+  if (D == 128)
+    return nqt == 1 ? launch_fwd<__half, 128, 128, 1>(mq, mk, mv, p, (int)grid, s)
+                    : launch_fwd<__half, 128, 128, 2>(mq, mk, mv, p, (int)grid, s);
+  return launch_fwd<__half, 192, 128, 2>(mq, mk, mv, p, (int)grid, s);
 }

@@ -218,7 +218,7 @@ def test_mla_projection_kernels_vs_torch(wdtype):
                               _lib.stream_of(q))
     _lib.check(st, "ffa_mla_q_absorb")
     q_ref = torch.cat([torch.einsum("rhd,hdl->rhl", q_nope.float(), w_uk.float()), rope(q_rope)], -1)
-    assert rel(q, q_ref.cpu().numpy()) <= 1e-2
+    assert rel(q, q_ref.detach().cpu().numpy()) <= 1e-2
     o_lat = torch.randn(R, H, L, device="cuda").to(torch.bfloat16)
     o = torch.full((R, H * (d + r)), 7.0, dtype=wdtype, device="cuda")
     st = lib.ffa_mla_o_absorb(o_lat.data_ptr(), _lib.i64arr(*o_lat.stride()[:2]), w_uv.data_ptr(),
@@ -226,7 +226,7 @@ def test_mla_projection_kernels_vs_torch(wdtype):
                               _lib.DTYPE_CODE[torch.bfloat16], R, H, d, L, r, _lib.stream_of(o))
     _lib.check(st, "ffa_mla_o_absorb")
     o_ref = torch.nn.functional.pad(torch.einsum("rhl,hdl->rhd", o_lat.float(), w_uv.float()), (0, r))
-    assert rel(o, o_ref.reshape(R, -1).cpu().numpy()) <= 1e-2
+    assert rel(o, o_ref.reshape(R, -1).detach().cpu().numpy()) <= 1e-2
     assert not o.view(R, H, d + r)[..., d:].any()
     # latent append into scattered slots
     slots = [3, 17, 40, 41, 127]
@@ -234,6 +234,6 @@ def test_mla_projection_kernels_vs_torch(wdtype):
     torch.cuda.synchronize()
     rows = dec.cache.pages.view(-1, L + r)
     ref_rows = torch.cat([lat.float(), rope(kr)], -1)
-    assert rel(rows[slots], ref_rows.cpu().numpy()) <= 1e-2
+    assert rel(rows[slots], ref_rows.detach().cpu().numpy()) <= 1e-2
     untouched = [i for i in range(rows.shape[0]) if i not in slots]
     assert not rows[untouched].any()
