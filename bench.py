@@ -332,6 +332,39 @@ def secondary_lines(dev, peaks, peak_src):
                               "gbs": mb / m_ms / 1e6, "frac_of_hbm": mb / m_ms / 1e6 / hbm,
                               "l2": "cache (75 MB) fits L2: flushed before every timed call",
                               "kernels": "ffa_mla_decode_tc_kernel + ffa_mla_merge_kernel"}
+    del cache, btm, lm, qm
+    # config 5 decode step end to end through MLADecoder.step (the Python
+    # included): one GEMM for the input projections, latent append + k RoPE,
+    # query absorption + q RoPE, the paged latent decode, value absorption,
+    # o_proj; 16 requests at context 4096 (the cache is filled directly).
+    from fastest_flash_attention_b200 import FastestFlashMLA, MLADecoder
+    torch.manual_seed(5)
+    mod = FastestFlashMLA(hidden_size=4096, num_heads=32, head_dim=128, latent_dim=512, rope_dim=64).to(dev).eval()
+    for prm in mod.parameters():
+        torch.nn.init.normal_(prm, std=0.02)
+    mod = mod.to(torch.bfloat16)
+    dec = MLADecoder(mod, max_pages=R * (L + 64) // PS + R, page_size=PS)
+    rows = dec.cache.pages.view(-1, 576)
+    for sid in range(R):
+        slots = torch.tensor(dec.cache._slots(sid, L), dtype=torch.long, device=dev)
+        rows[slots] = torch.randn(L, 576, device=dev, dtype=torch.bfloat16)
+    x = torch.randn(R, 1, 4096, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        dec.step(x, list(range(R)))
+    torch.cuda.synchronize(dev)
+    n_steps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_steps):
+        dec.step(x, list(range(R)))
+    e1.record()
+    torch.cuda.synchronize(dev)
+    st_ms = e0.elapsed_time(e1) / n_steps
+    out["mla_decode_step_cfg5"] = {
+        "workload": "MLADecoder.step, 16 requests, context 4096 -> 4116, hidden 4096, 32 heads, latent 512 + rope 64, "
+                    "bf16 weights N(0, 0.02)", "ms_per_step": st_ms, "tokens_per_s": R / st_ms * 1e3,
+        "timing": "CUDA events around 20 consecutive steps, host work included (the cache grows by a token per step)"}
+    del dec, mod
     return out
 
 
@@ -344,6 +377,48 @@ def rank_blocks(world: int, rank: int):
 def block_flops(blocks) -> float:
     G = CFG["Hq"] // CFG["Hkv"]
     return sum(fwd_flops(b1 - b0, (h1 - h0) * G, CFG["S"], CFG["D"]) for b0, b1, h0, h1 in blocks)
+
+
+def pcie_ceiling(dev, qp, q_d, o_host, stream, h2d, d2h):
+    """Pinned-host copy bandwidth of this GPU's link, measured with the e2e
+    leg's own buffers: H2D alone, D2H alone, and both at once on two streams.
+    The e2e step cannot beat moving its bytes: ceiling = max(h2d / H2D rate,
+    d2h / D2H rate) with the directions overlapped (the step's pipeline), and
+    the slower of that and the sum if the link cannot run both at full rate."""
+    nb = min(qp.numel(), o_host.numel())
+    src_h, dst_d = qp.view(-1)[:nb], q_d.view(-1)[:nb]
+    dst_h = o_host.view(-1)[:nb]
+    byts = nb * 2
+    s2 = torch.cuda.Stream(dev)
+
+    def timed(fn, reps=5):
+        fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / reps
+
+    t_h2d = timed(lambda: dst_d.copy_(src_h, non_blocking=True))
+    t_d2h = timed(lambda: dst_h.copy_(dst_d, non_blocking=True))
+
+    def both():
+        s2.wait_stream(stream)
+        dst_d.copy_(src_h, non_blocking=True)
+        with torch.cuda.stream(s2):
+            dst_h.copy_(q_d.view(-1)[:nb], non_blocking=True)
+        stream.wait_stream(s2)
+    t_both = timed(both)
+    h2d_gbs, d2h_gbs = byts / t_h2d / 1e6, byts / t_d2h / 1e6
+    overlapped = max(h2d / (h2d_gbs * 1e6), d2h / (d2h_gbs * 1e6))
+    # both directions together: bytes moved per ms when each direction copies `byts`
+    both_gbs = 2 * byts / t_both / 1e6
+    ceiling = max(overlapped, (h2d + d2h) / (both_gbs * 1e6))
+    return {"h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs, "bidirectional_gbs": both_gbs, "ceiling_ms": ceiling,
+            "how": f"{byts / 1e6:.0f} MB pinned copies with the e2e buffers, CUDA events, mean of 5"}
 
 
 def multi_gpu_lines(dev, world, rank, peaks, peak_src):
@@ -520,6 +595,7 @@ def run_ours(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
     e2e_val = flops / (e2e_ms * 1e-3) / 1e12
     _lib.check_device_errors(dev)
+    link = pcie_ceiling(dev, qp, q_d, o_host, stream, h2d, d2h)
 
     peaks, peak_src = load_peaks()
     del parts, q_d, k_d, v_d
@@ -540,6 +616,8 @@ def run_ours(args, world, rank, local):
         "config": workload_config(world),
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "bytes_are": "rank 0's copies (every rank moves its own groups' share)",
+                "link": link,
+                "frac_of_link_ceiling": (link["ceiling_ms"] / e2e_ms) if link.get("ceiling_ms") else None,
                 "api": "fastest_flash_attn_forward(causal=True, return_lse=True) per (batch element, half its kv "
                        "heads with their query-head groups); H2D, forward and D2H pipelined on three streams"},
         "gpu_launches": args.steps * len(blocks),

@@ -36,6 +36,8 @@
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
+#include <type_traits>
+
 namespace ffa {
 
 constexpr int BWD_BT = 128;       // rows of the tile a CTA keeps (keys in dK/dV, queries in dQ)
@@ -135,16 +137,17 @@ __device__ __forceinline__ uint32_t block_mask_bits32(int x0, int bs, int nb, Ce
 // P and dS for 16 columns of one TMEM row.  s: raw Q.K scores, dp: dO.V
 // values.  Minus the base-2 LSE and Delta of each column come from smem
 // (COL_STATS, dK/dV kernel: cnl2 / cdl, 16-byte aligned) or are the row's
-// (rnl2 / rdl, dQ kernel).  With MASKED, columns c whose bit c of `keep` is
-// clear are dropped (P = dS = 0).  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
+// (rnl2 / rdl, dQ kernel).  With MASKED, columns c with (uint)(c - lo) >= cnt
+// are dropped, and with BITS also those whose bit c of `bits` is clear (the
+// block mask).  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
 // pipe); 2: softcap with tanh through ex2 / rcp.  Columns are processed in
 // pairs with packed fp32x2 instructions (per lane the same IEEE operations as
 // the scalar forms: dp - dl is computed as dp + dl * -1, and
 // (dp - dl)(1 - th^2) as (dl - dp)(th^2 - 1), both exact rewrites).
-template <typename T, bool WRITE_P, bool COL_STATS, int MODE, bool MASKED>
+template <typename T, bool WRITE_P, bool COL_STATS, int MODE, bool MASKED, bool BITS>
 __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
-                                            const float* cnl2, const float* cdl, float rnl2, float rdl,
-                                            uint32_t keep, uint32_t* pk_p, uint32_t* pk_ds) {
+                                            const float* cnl2, const float* cdl, float rnl2, float rdl, int lo,
+                                            uint32_t cnt, uint32_t bits, uint32_t* pk_p, uint32_t* pk_ds) {
 #pragma unroll
   for (int c4 = 0; c4 < 16; c4 += 4) {
     float2 nl2[2], dl[2];
@@ -179,8 +182,12 @@ __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* 
       }
       float2 pr = make_float2(ex2(x.x), ex2(x.y));
       if (MASKED) {
-        pr.x = ((keep >> c) & 1u) ? pr.x : 0.f;
-        pr.y = ((keep >> (c + 1)) & 1u) ? pr.y : 0.f;
+        pr.x = ((uint32_t)(c - lo) < cnt) ? pr.x : 0.f;
+        pr.y = ((uint32_t)(c + 1 - lo) < cnt) ? pr.y : 0.f;
+        if (BITS) {
+          pr.x = ((bits >> c) & 1u) ? pr.x : 0.f;
+          pr.y = ((bits >> (c + 1)) & 1u) ? pr.y : 0.f;
+        }
       }
       const float2 dv = fmul2(pr, g);
       if (WRITE_P) pk_p[c / 2] = pack2<T>(pr.x, pr.y);
@@ -189,12 +196,13 @@ __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* 
   }
 }
 
-template <typename T, bool WRITE_P, bool COL_STATS, bool MASKED>
+template <typename T, bool WRITE_P, bool COL_STATS, bool MASKED, bool BITS>
 __device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint32_t* s, const uint32_t* dp,
                                                  const float* cnl2, const float* cdl, float rnl2, float rdl,
-                                                 uint32_t keep, uint32_t* pk_p, uint32_t* pk_ds) {
+                                                 int lo, uint32_t cnt, uint32_t bits, uint32_t* pk_p,
+                                                 uint32_t* pk_ds) {
   if (!p.use_softcap) {
-    bwd_chunk16<T, WRITE_P, COL_STATS, 0, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 0, MASKED, BITS>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, bits, pk_p, pk_ds);
     return;
   }
   // The cap is usually far above the scores, so tanh's argument is small:
@@ -203,9 +211,9 @@ __device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint3
 #pragma unroll
   for (int c = 0; c < 16; c += 2) mx = fmax3(mx, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
   if (__all_sync(0xffffffffu, mx <= p.sc_small))
-    bwd_chunk16<T, WRITE_P, COL_STATS, 1, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 1, MASKED, BITS>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, bits, pk_p, pk_ds);
   else
-    bwd_chunk16<T, WRITE_P, COL_STATS, 2, MASKED>(p, s, dp, cnl2, cdl, rnl2, rdl, keep, pk_p, pk_ds);
+    bwd_chunk16<T, WRITE_P, COL_STATS, 2, MASKED, BITS>(p, s, dp, cnl2, cdl, rnl2, rdl, lo, cnt, bits, pk_p, pk_ds);
 }
 
 // Stores 16-byte chunk `chunk` of row `row` of a 128-byte-swizzled K-major
@@ -223,16 +231,17 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, uint
 // (Releasing S before dP is read was measured slower: the two loads then
 // no longer overlap.)
 // Column statistics come from smem (COL_STATS: cnl2 / cdl for the first
-// column) or are the row's (rnl2, rdl).  The row keeps the columns whose bit
-// is set in `keep` (bit c = column c of the 32); `masked` (warp-uniform) is
-// false when no row of the warp drops any column.  Before storing, waits (if pt_parity >= 0)
+// column) or are the row's (rnl2, rdl).  The row keeps columns
+// [keep_lo, keep_hi] of the 32 (and, with BM, only those whose bit is set in
+// `bm_bits`, from the block mask); `masked` (warp-uniform) is false when no
+// row of the warp drops any column.  Before storing, waits (if pt_parity >= 0)
 // for `pt_free` to show that the smem tiles' previous contents were consumed;
 // then P^T (WRITE_P) goes to sP and dS to sDS, as 16-byte chunks
 // 4*half .. 4*half+3 of the row.  Returns false if that wait gave up.
-template <typename T, bool WRITE_P, bool COL_STATS>
+template <typename T, bool WRITE_P, bool COL_STATS, bool BM>
 __device__ __forceinline__ bool bwd_unit(const BwdParams& p, uint32_t tS, uint32_t tDP, uint64_t* tmem_free,
-                                         const float* cnl2, const float* cdl, float rnl2, float rdl,
-                                         uint32_t keep, bool masked, uint64_t* pt_free, int pt_parity,
+                                         const float* cnl2, const float* cdl, float rnl2, float rdl, int keep_lo,
+                                         int keep_hi, uint32_t bm_bits, bool masked, uint64_t* pt_free, int pt_parity,
                                          volatile int* abort_flag, uint8_t* sP, uint8_t* sDS, int row, int half) {
   uint32_t s[32], d[32];
   tmem_ld32(tS, s);
@@ -248,11 +257,14 @@ __device__ __forceinline__ bool bwd_unit(const BwdParams& p, uint32_t tS, uint32
     const float* n2 = COL_STATS ? cnl2 + 16 * k : nullptr;
     const float* d2 = COL_STATS ? cdl + 16 * k : nullptr;
     if (masked) {
-      bwd_chunk16_mode<T, WRITE_P, COL_STATS, true>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl,
-                                                    (keep >> (16 * k)) & 0xffffu, pp + 8 * k, pd + 8 * k);
+      const int lo = max(keep_lo - 16 * k, 0);
+      const int z = min(keep_hi - 16 * k, 15);
+      const uint32_t cnt = z >= lo ? (uint32_t)(z - lo + 1) : 0u;
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, true, BM>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, lo, cnt,
+                                                        bm_bits >> (16 * k), pp + 8 * k, pd + 8 * k);
     } else {
-      bwd_chunk16_mode<T, WRITE_P, COL_STATS, false>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, 0xffffu,
-                                                     pp + 8 * k, pd + 8 * k);
+      bwd_chunk16_mode<T, WRITE_P, COL_STATS, false, false>(p, s + 16 * k, d + 16 * k, n2, d2, rnl2, rdl, 0, 16u,
+                                                            0u, pp + 8 * k, pd + 8 * k);
     }
   }
   if (pt_parity >= 0 &&
@@ -550,7 +562,7 @@ struct DkdvCfg {
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-template <typename T, int D, int DV>
+template <typename T, int D, int DV, bool BM>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     ffa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -724,16 +736,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_after();
       const int s = u % NS;
       const int q0 = (i_lo + u % n_i) * BWD_BS + 32 * half;
-      uint32_t keep = range_bits32(q_keep_lo - q0, q_keep_hi - q0);
-      if (p.block_mask != nullptr && key < p.Skv) {  // queries are the mask's rows here
+      const int keep_lo = q_keep_lo - q0, keep_hi = q_keep_hi - q0;
+      uint32_t bm_bits = ~0u;
+      if (BM && key < p.Skv) {  // queries are the block mask's rows here
         const uint8_t* mcol = p.block_mask + key / p.mask_bkv;
-        keep &= block_mask_bits32(q0, p.mask_bq, p.n_br, [&](int br) { return mcol[(size_t)br * p.n_bc] != 0; });
+        bm_bits = block_mask_bits32(q0, p.mask_bq, p.n_br, [&](int br) { return mcol[(size_t)br * p.n_bc] != 0; });
       }
-      const bool masked = !__all_sync(0xffffffffu, keep == ~0u);
+      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31 && (!BM || bm_bits == ~0u));
       const float* nl2 = sStat + 2 * BWD_BS * s + 32 * half;
       // this pair's P^T / dS^T smem tiles are free once unit u-2's accumulation MMAs are done
-      ok = bwd_unit<T, true, true>(p, tS, tDP, &bars->tmem_free[pair], nl2, nl2 + BWD_BS, 0.f, 0.f, keep,
-                                   masked, &bars->pt_free[pair], u >= 2 ? ((u - 2) >> 1) & 1 : -1,
+      ok = bwd_unit<T, true, true, BM>(p, tS, tDP, &bars->tmem_free[pair], nl2, nl2 + BWD_BS, 0.f, 0.f, keep_lo,
+                                       keep_hi, bm_bits, masked, &bars->pt_free[pair], u >= 2 ? ((u - 2) >> 1) & 1 : -1,
                                    abort_flag, sPT + pair * Cfg::PT, sPT + (2 + pair) * Cfg::PT, r, half);
       if (lane == 0) mbar_arrive(&bars->ds_ready[pair]);
     }
@@ -817,7 +830,7 @@ struct DqCfg {
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-template <typename T, int D, int DV>
+template <typename T, int D, int DV, bool BM>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1001,14 +1014,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       const int c0 = (j_lo + u) * UK + colw;
-      uint32_t keep = range_bits32(k_keep_lo - c0, k_keep_hi - c0);
-      if (p.block_mask != nullptr) {  // keys are the mask's columns here
+      const int keep_lo = k_keep_lo - c0, keep_hi = k_keep_hi - c0;
+      uint32_t bm_bits = ~0u;
+      if (BM) {  // keys are the block mask's columns here
         const uint8_t* mrow = p.block_mask + (size_t)(min(row, p.Sq - 1) / p.mask_bq) * p.n_bc;
-        keep &= block_mask_bits32(c0, p.mask_bkv, p.n_bc, [&](int bc) { return mrow[bc] != 0; });
+        bm_bits = block_mask_bits32(c0, p.mask_bkv, p.n_bc, [&](int bc) { return mrow[bc] != 0; });
       }
-      const bool masked = !__all_sync(0xffffffffu, keep == ~0u);
-      ok = bwd_unit<T, false, false>(p, tS, tDP, &bars->tmem_free[bb], nullptr, nullptr, row_nl2, row_dl,
-                                     keep, masked, &bars->pt_free[bb],
+      const bool masked = !__all_sync(0xffffffffu, keep_lo <= 0 && keep_hi >= 31 && (!BM || bm_bits == ~0u));
+      ok = bwd_unit<T, false, false, BM>(p, tS, tDP, &bars->tmem_free[bb], nullptr, nullptr, row_nl2, row_dl,
+                                         keep_lo, keep_hi, bm_bits, masked, &bars->pt_free[bb],
                                      u >= 2 ? ((u - 2) >> 1) & 1 : -1, abort_flag, nullptr, sDSw + bb * Cfg::DS, r,
                                      chunk_half);
       if (lane == 0) mbar_arrive(&bars->ds_ready[bb]);
@@ -1040,7 +1054,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
-template <typename T, int D, int DV>
+template <typename T, int D, int DV, bool BM>
 static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o, const void* dout,
                       const float* lse, float* lse2, float* delta, const int64_t* o_str, const int64_t* do_str,
                       cudaStream_t st) {
@@ -1072,7 +1086,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
   if (s) return s;
   // 2. dK / dV
   {
-    auto kern = ffa_bwd_dkdv_kernel<T, D, DV>;
+    auto kern = ffa_bwd_dkdv_kernel<T, D, DV, BM>;
     static std::atomic<uint64_t> done{0};
     if ((s = smem_attr_once(kern, DkdvCfg<D, DV>::SMEM, done))) return s;
     const int grid = (p.Skv + BWD_BT - 1) / BWD_BT * p.B * p.Hkv;
@@ -1081,7 +1095,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
   }
   // 3. dQ
   {
-    auto kern = ffa_bwd_dq_kernel<T, D, DV>;
+    auto kern = ffa_bwd_dq_kernel<T, D, DV, BM>;
     static std::atomic<uint64_t> done{0};
     if ((s = smem_attr_once(kern, DqCfg<D, DV>::SMEM, done))) return s;
     const int grid = (p.Sq + BWD_BT - 1) / BWD_BT * p.B * p.Hq;
@@ -1183,15 +1197,23 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
                       64, BWD_BS);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == FFA_DTYPE_BF16) {
-    if (D == 64) return launch_bwd<__nv_bfloat16, 64, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+  auto run = [&](auto bm) -> int {
+    constexpr bool BM = decltype(bm)::value;
+    if (dtype == FFA_DTYPE_BF16) {
+      if (D == 64)
+        return launch_bwd<__nv_bfloat16, 64, 64, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+      if (D == 128)
+        return launch_bwd<__nv_bfloat16, 128, 128, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+      return launch_bwd<__nv_bfloat16, 192, 128, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+    }
+    if (D == 64) return launch_bwd<__half, 64, 64, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
     if (D == 128)
-      return launch_bwd<__nv_bfloat16, 128, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-    return launch_bwd<__nv_bfloat16, 192, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-  }
-  if (D == 64) return launch_bwd<__half, 64, 64>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-  if (D == 128) return launch_bwd<__half, 128, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
-  return launch_bwd<__half, 192, 128>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+      return launch_bwd<__half, 128, 128, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+    return launch_bwd<__half, 192, 128, BM>(maps, p, o, dout, lse, lse2, delta, o_strides, do_strides, s);
+  };
+  // Block-mask support is compiled into its own kernels, so the unmasked
+  // kernels carry none of its per-unit work.
+  return block_mask ? run(std::true_type{}) : run(std::false_type{});
 }
 
 extern "C" int ffa_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o,
