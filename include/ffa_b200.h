@@ -52,7 +52,11 @@ int ffa_version(void);
 const char* ffa_last_error(void);
 
 /* Device error word helpers: kernels record the site code of an expired wait
- * into a caller-provided uint32 in device memory (nullptr disables it).
+ * into a caller-provided uint32 in device memory (nullptr disables it), and
+ * invalid data they find: 0x3E0 a decode context length outside
+ * [0, max_pages_per_req * page_size], 0x3E1 a block-table page id outside
+ * [0, num_pages), 0x1FF a block mask keeping more key tiles than the forward's
+ * tile list holds (the offending loads are skipped; treat the call as failed).
  * ffa_read_error copies it to *out (synchronising `stream`). */
 int ffa_read_error(const uint32_t* dev_err, uint32_t* out, void* stream);
 
