@@ -207,3 +207,33 @@ def test_backward_with_block_mask(S, Skv, D, bs, causal, window):
         t.grad = None
     m.fastest_flash_attn_func(qc, kc, vc, None, causal, bs, None, window, False, bm).backward(do.cuda())
     assert all(torch.equal(a, t.grad) for a, t in zip(g1, (qc, kc, vc)))
+
+
+def test_config3_full_size_sampled_heads():
+    """Config 3 at full size (B=8 H=16 S=4096 D=128, causal + window 1024 +
+    softcap 30, bf16, dO ~ N(0,1)): one fwd+bwd of the whole batch through the
+    autograd function, bit-identical when repeated, and dq/dk/dv of sampled
+    (batch, head) slices against fp32 torch autograd of the same attention."""
+    m = ffa()
+    B, H, S, D, W, cap = 8, 16, 4096, 128, 1024, 30.0
+    g = torch.Generator(device="cuda").manual_seed(21)
+    q, k, v, do = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    qc, kc, vc = (t.clone().requires_grad_(True) for t in (q, k, v))
+    m.fastest_flash_attn_func(qc, kc, vc, causal=True, sliding_window=W, softcap=cap).backward(do)
+    grads = [t.grad.clone() for t in (qc, kc, vc)]
+    for t in (qc, kc, vc):
+        t.grad = None
+    m.fastest_flash_attn_func(qc, kc, vc, causal=True, sliding_window=W, softcap=cap).backward(do)
+    assert all(torch.equal(a, t.grad) for a, t in zip(grads, (qc, kc, vc)))
+    i = torch.arange(S, device="cuda")
+    keep = (i[None, :] <= i[:, None]) & (i[None, :] > i[:, None] - W)
+    for b, h in ((0, 0), (3, 7), (7, 15)):
+        qf, kf, vf = (t[b, h].float().requires_grad_(True) for t in (q, k, v))
+        s = (qf @ kf.T) / math.sqrt(D)
+        s = cap * torch.tanh(s / cap)
+        o = torch.softmax(s.masked_fill(~keep, float("-inf")), -1) @ vf
+        o.backward(do[b, h].float())
+        for got, ref, nm in ((grads[0][b, h], qf.grad, "dq"), (grads[1][b, h], kf.grad, "dk"),
+                             (grads[2][b, h], vf.grad, "dv")):
+            e = (got.float() - ref).abs().max().item() / ref.abs().max().item()
+            assert e <= G_TOL, f"({b},{h}) {nm}: rel err {e:.3e}"
