@@ -179,6 +179,16 @@ def main() -> None:
                               inv_freq=N(mla.rope.inv_freq),
                               params=np.array(repr(dict(num_heads=2, head_dim=64, rope_dim=16, block_size=16))))
 
+    # ---- small head dims (the sizes the reference's own tests use) ----
+    # (after every other case, so the random streams of those stay unchanged)
+    fwd_case("fwd_small_d4_causal", 2, 2, 2, 33, 33, 4, causal=True, block_size=8)
+    fwd_case("fwd_small_d8_window_softcap", 1, 4, 2, 50, 50, 8, causal=True, sliding_window=12, softcap=5.0,
+             block_size=16)
+    fwd_case("fwd_small_d32_mqa_sq_ne_skv", 1, 4, 1, 17, 45, 32, block_size=16)
+    bwd_case("bwd_small_d8_causal", 2, 2, 40, 8, causal=True, block_size=16)
+    bwd_case("bwd_small_d16_window", 1, 2, 70, 16, causal=True, sliding_window=20, block_size=16)
+    bwd_case("bwd_small_d32_softcap", 1, 1, 64, 32, softcap=10.0, block_size=32)
+
     out.mkdir(parents=True, exist_ok=True)
     total = 0
     for name, arrs in cases.items():

@@ -32,7 +32,8 @@ def rel_err(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-6))
 
 
-@pytest.mark.parametrize("name", ["bwd_causal_d64", "bwd_window_softcap_d128", "bwd_noncausal_d64"])
+@pytest.mark.parametrize("name", ["bwd_causal_d64", "bwd_window_softcap_d128", "bwd_noncausal_d64",
+                                  "bwd_small_d8_causal", "bwd_small_d16_window", "bwd_small_d32_softcap"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_backward_matches_reference_golden(name, dtype):
     g = load_golden(name)

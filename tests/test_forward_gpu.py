@@ -37,7 +37,9 @@ def close(a, b, tol, what):
 
 
 GOLDEN_FWD = ["fwd_basic_d16", "fwd_causal_d64", "fwd_causal_d128_ragged", "fwd_window_d64", "fwd_softcap_d64", "fwd_gqa_d128",
-              "fwd_noncausal_sq_ne_skv_d64", "fwd_two_pass_d64", "fwd_blockmask_d64"]
+              "fwd_noncausal_sq_ne_skv_d64", "fwd_two_pass_d64", "fwd_blockmask_d64",
+              # the reference's own test sizes (D = 4 / 8 / 32), zero-padded onto the D = 64 kernel
+              "fwd_small_d4_causal", "fwd_small_d8_window_softcap", "fwd_small_d32_mqa_sq_ne_skv"]
 
 
 @pytest.mark.parametrize("name", GOLDEN_FWD)

@@ -10,7 +10,8 @@ from oracle import attention_oracle as O
 
 FWD_CASES = ["fwd_basic_d16", "fwd_causal_d64", "fwd_causal_d128_ragged", "fwd_window_d64", "fwd_softcap_d64",
              "fwd_gqa_d128", "fwd_noncausal_sq_ne_skv_d64", "fwd_two_pass_d64", "fwd_blockmask_d64",
-             "fwd_fp16_compute_d16"]
+             "fwd_fp16_compute_d16", "fwd_small_d4_causal", "fwd_small_d8_window_softcap",
+             "fwd_small_d32_mqa_sq_ne_skv"]
 
 
 def _fwd_kwargs(p):
@@ -39,7 +40,8 @@ def test_forward_kvcache_matches_reference():
     np.testing.assert_allclose(lse, g["lse"], atol=2e-5)
 
 
-@pytest.mark.parametrize("name", ["bwd_causal_d64", "bwd_window_softcap_d128", "bwd_noncausal_d64"])
+@pytest.mark.parametrize("name", ["bwd_causal_d64", "bwd_window_softcap_d128", "bwd_noncausal_d64",
+                                  "bwd_small_d8_causal", "bwd_small_d16_window", "bwd_small_d32_softcap"])
 def test_backward_matches_reference(name):
     g = load_golden(name)
     p = golden_params(g)
