@@ -379,6 +379,31 @@ def block_flops(blocks) -> float:
     return sum(fwd_flops(b1 - b0, (h1 - h0) * G, CFG["S"], CFG["D"]) for b0, b1, h0, h1 in blocks)
 
 
+def e2e_chunks(blocks, kv_chunk: int):
+    """(batch element, kv-head range) chunks of this rank's groups for the e2e
+    pipeline: kv_chunk heads each, except that the first and the last chunk
+    are cut down to single kv heads.  The first forward can start only once
+    its inputs have crossed PCIe, and the last chunk's forward and output copy
+    run after all inputs have arrived: small end chunks shorten both exposed
+    ends while the middle keeps chunks large enough to hide the per-call host
+    work behind the copies."""
+    base = [(b, g0, min(g0 + kv_chunk, h1)) for b0, b1, h0, h1 in blocks for b in range(b0, b1)
+            for g0 in range(h0, h1, kv_chunk)]
+
+    def split(c, first):
+        b, g0, g1 = c
+        n = g1 - g0
+        if n <= 2:
+            return [(b, g, g + 1) for g in range(g0, g1)]
+        if first:  # 1, 1, then the rest
+            return [(b, g0, g0 + 1), (b, g0 + 1, g0 + 2), (b, g0 + 2, g1)]
+        return [(b, g0, g1 - 2), (b, g1 - 2, g1 - 1), (b, g1 - 1, g1)]
+
+    if len(base) == 1:
+        return split(base[0], True)
+    return split(base[0], True) + base[1:-1] + split(base[-1], False)
+
+
 def pcie_ceiling(dev, qp, q_d, o_host, stream, h2d, d2h):
     """Pinned-host copy bandwidth of this GPU's link, measured with the e2e
     leg's own buffers: H2D alone, D2H alone, and both at once on two streams.
@@ -544,18 +569,17 @@ def run_ours(args, world, rank, local):
     lse_host = torch.empty((B, Hq, S, 1), dtype=torch.float32).pin_memory()
 
     # Chunks of one batch element and half its kv heads (each kv head with its
-    # group of query heads: complete GQA attention problems), restricted to
-    # this rank's groups, on three streams: the H2D copy of chunk c+1 and the
-    # D2H copy of chunk c-1 overlap the forward of chunk c, so the step costs
-    # about the PCIe time of the inputs plus one chunk.  (Smaller chunks were
-    # measured slower: the host-side call overhead then no longer hides behind
-    # the copies.)  Device input buffers are allocated once, outside the timed
+    # group of query heads: complete GQA attention problems; the first and
+    # last chunks smaller, see e2e_chunks), restricted to this rank's groups,
+    # on three streams: the H2D copy of chunk c+1 and the D2H copy of chunk c-1
+    # overlap the forward of chunk c, so the step costs about the PCIe time of
+    # the inputs plus a small chunk.  (Uniformly smaller chunks were measured
+    # slower: the host-side call overhead then no longer hides behind the
+    # copies.)  Device input buffers are allocated once, outside the timed
     # region; every byte of input and output still crosses PCIe inside it.
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     q_d, k_d, v_d = (torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (qp, kp, vp))
-    KV_CHUNK = max(1, Hkv // 2)
-    chunks = [(b, g0, min(g0 + KV_CHUNK, h1)) for b0, b1, h0, h1 in blocks for b in range(b0, b1)
-              for g0 in range(h0, h1, KV_CHUNK)]
+    chunks = e2e_chunks(blocks, max(1, Hkv // 2))
     h2d = sum((qp[b, g0 * G:g1 * G].numel() + 2 * kp[b, g0:g1].numel()) * 2 for b, g0, g1 in chunks)
     d2h = sum(o_host[b, g0 * G:g1 * G].numel() * 2 + lse_host[b, g0 * G:g1 * G].numel() * 4 for b, g0, g1 in chunks)
 
