@@ -240,3 +240,24 @@ def test_cpu_tensors_raise():
     q = torch.randn(1, 1, 8, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         ffa().fastest_flash_attn_forward(q, q, q)
+
+
+def test_two_devices_in_one_process():
+    """The kernels' shared-memory attribute is per device: forward and backward
+    on cuda:0 then cuda:1 (then cuda:0 again) from one process all run and
+    agree with fp32 torch."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    m = ffa()
+    for d in (0, 1, 0):
+        dev = torch.device("cuda", d)
+        g = torch.Generator(device=dev).manual_seed(d)
+        q, k, v = (torch.randn(1, 2, 300, 128, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+                   for _ in range(3))
+        o = m.fastest_flash_attn_func(q, k, v, causal=True)
+        o.float().sum().backward()
+        s = (q.float() @ k.float().transpose(-1, -2)) / math.sqrt(128)
+        s = s.masked_fill(torch.ones(300, 300, device=dev, dtype=torch.bool).triu(1), float("-inf"))
+        ro = torch.softmax(s, -1) @ v.float()
+        assert (o.float() - ro).abs().max().item() <= O_TOL
+        assert q.grad is not None and torch.isfinite(q.grad.float()).all()
