@@ -562,10 +562,14 @@ struct DkdvCfg {
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
+// The dK/dV epilogue at D = DV = 128 stages 16 warp boxes of 4 KB in the stage smem.
+static_assert(DkdvCfg<128, 128>::NS * DkdvCfg<128, 128>::STAGE >= 16 * 32 * 128, "dK/dV store staging");
+
 template <typename T, int D, int DV, bool BM>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     ffa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                        const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
                         const BwdParams p) {
   using Cfg = DkdvCfg<D, DV>;
   constexpr int NS = Cfg::NS;
@@ -762,17 +766,51 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t tacc = tmem + lane_off + TM_ACC + pair * DV;
     const float mul = pair ? p.scale : 1.f;
     const int ncol = pair ? D : DV;
+    if (D == 128 && DV == 128 && (have || n == 0)) {
+      // Each warp packs its 32 rows x 64 columns into the (now idle) stage
+      // smem in the 128-byte-swizzled layout and hands them to one TMA store,
+      // so the CTA leaves once the copy has read the smem instead of once
+      // every row's global stores have been issued.
+      uint8_t* tile = sStage + (size_t)(wg * 4 + warp % 4) * (32 * 128);
+      const int lr = r % 32;
 #pragma unroll 1
-    for (int c = half * (ncol / 2); c < (half + 1) * (ncol / 2); c += 32) {
-      uint32_t v[32];
-      if (have) {
-        tmem_ld32(tacc + c, v);
-        tmem_ld_wait32(v);
-      } else {
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t v[32];
+        if (have) {
+          tmem_ld32(tacc + half * 64 + c, v);
+          tmem_ld_wait32(v);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = 0u;
+          for (int e = 0; e < 32; ++e) v[e] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack2<T>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) st_sw128(tile, lr, c / 8 + q, pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
-      store_row32<T>(row + c, v, mul, store);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_4d(pair == 0 ? &tmDV : &tmDK, tile, half * 64, j * BWD_BT + (warp % 4) * 32, hkv, b);
+        tma_store_commit();
+        tma_store_wait_read();
+      }
+      __syncwarp();
+    } else {
+#pragma unroll 1
+      for (int c = half * (ncol / 2); c < (half + 1) * (ncol / 2); c += 32) {
+        uint32_t v[32];
+        if (have) {
+          tmem_ld32(tacc + c, v);
+          tmem_ld_wait32(v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0u;
+        }
+        store_row32<T>(row + c, v, mul, store);
+      }
     }
   }
   tc_fence_before();
@@ -1090,7 +1128,7 @@ static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o
     static std::atomic<uint64_t> done{0};
     if ((s = smem_attr_once(kern, DkdvCfg<D, DV>::SMEM, done))) return s;
     const int grid = (p.Skv + BWD_BT - 1) / BWD_BT * p.B * p.Hkv;
-    kern<<<grid, BWD_THREADS, DkdvCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], p);
+    kern<<<grid, BWD_THREADS, DkdvCfg<D, DV>::SMEM, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
     if ((s = launch_status())) return s;
   }
   // 3. dQ
@@ -1183,7 +1221,7 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
 
   const CUtensorMapDataType dt =
       dtype == FFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap maps[4];
+  CUtensorMap maps[6];
   int st = make_tmap_4d(&maps[0], q, dt, 2, D, Sq, Hq, B, q_strides[2] * 2, q_strides[1] * 2, q_strides[0] * 2, 64,
                         BWD_BS);
   if (!st)
@@ -1195,6 +1233,13 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
   if (!st)
     st = make_tmap_4d(&maps[3], dout, dt, 2, Dv, Sq, Hq, B, do_strides[2] * 2, do_strides[1] * 2, do_strides[0] * 2,
                       64, BWD_BS);
+  // dK / dV stores: one 32-row x 64-column box per warp
+  if (!st)
+    st = make_tmap_4d(&maps[4], dk, dt, 2, D, Skv, Hkv, B, dk_strides[2] * 2, dk_strides[1] * 2, dk_strides[0] * 2,
+                      64, 32);
+  if (!st)
+    st = make_tmap_4d(&maps[5], dv, dt, 2, Dv, Skv, Hkv, B, dv_strides[2] * 2, dv_strides[1] * 2, dv_strides[0] * 2,
+                      64, 32);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto run = [&](auto bm) -> int {
