@@ -202,7 +202,7 @@ def run_reference(args, world, rank):
     vals = []
     sample = ""
     for i in range(args.warmup + args.steps):
-        tf, dt, sample = cpu_reference_sample(q, k, v)
+        tf, dt, sample = cpu_reference_sample(q, k, v, heads=8)
         if i >= args.warmup:
             vals.append(tf)
     value = statistics.median(vals)
@@ -295,6 +295,7 @@ def secondary_lines(dev, peaks, peak_src):
     out["train_fwd_bwd_cfg3"] = {
         "workload": "B=8 H=16 S=4096 D=128 causal+window1024+softcap30, deterministic bwd",
         "fwd_ms": f_ms, "bwd_ms": b_ms, "fwd_tflops": ff / f_ms / 1e9, "bwd_tflops": 2.5 * ff / b_ms / 1e9,
+        "train_tokens_per_s": B * S / ((f_ms + b_ms) * 1e-3),
         "fwd_bwd_tflops": 3.5 * ff / (f_ms + b_ms) / 1e9,
         "frac_of_peak": 3.5 * ff / (f_ms + b_ms) / 1e9 / pk, "peak": f"{pk} TFLOP/s ({peak_src} bf16)"}
     del q, k, v, do, o, lse
@@ -305,7 +306,7 @@ def secondary_lines(dev, peaks, peak_src):
     out["paged_decode_cfg4"] = {
         "workload": "64 req, ctx U[512,32768], page 16, Hq 32 / Hkv 8, D 128, bf16, permuted block table",
         "ms": d_ms, "gbs": byts / d_ms / 1e6, "frac_of_hbm": byts / d_ms / 1e6 / hbm,
-        "bytes": byts, "peak": f"{hbm} GB/s ({peak_src})"}
+        "requests_per_s": 64 / d_ms * 1e3, "bytes": byts, "peak": f"{hbm} GB/s ({peak_src})"}
     del q, kp, vp
     # config 5 prefill: the MLA module's attention at (qk 192, v 128), B=16 H=32 S=4096 causal
     B5, H5, S5 = 16, 32, 4096
@@ -637,7 +638,7 @@ def run_ours(args, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*D^-1/4)",
-        "config": workload_config(world),
+        "tokens_per_s": B * S / (ms * 1e-3), "config": workload_config(world),
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "bytes_are": "rank 0's copies (every rank moves its own groups' share)",
                 "link": link,
@@ -657,7 +658,8 @@ def run_ours(args, world, rank, local):
         if multi:
             line["secondary"].update(multi)
     if world == 1:
-        runs = [cpu_reference_sample(q_h, k_h, v_h) for _ in range(3)]
+        # about 10-15 s of CPU work: 16 query heads (half of batch element 0), 3 runs
+        runs = [cpu_reference_sample(q_h, k_h, v_h, heads=16) for _ in range(3)]
         tfc = statistics.median(r[0] for r in runs)
         line["cpu_baseline"] = {"value": tfc, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
                                 "sample": runs[0][2] + ", median of 3",
