@@ -29,15 +29,9 @@
 namespace ffa {
 
 constexpr int DEC_CHUNK = 16;     // tokens per chunk (one MMA K-step of P V)
-#ifndef FFA_DEC_CONSUMERS
-#define FFA_DEC_CONSUMERS 4
-#endif
-#ifndef FFA_DEC_STAGES
-#define FFA_DEC_STAGES 8
-#endif
-constexpr int DEC_CONSUMERS = FFA_DEC_CONSUMERS;  // consumer warps
+constexpr int DEC_CONSUMERS = 4;  // consumer warps
 constexpr int DEC_THREADS = (DEC_CONSUMERS + 1) * 32;
-constexpr int DEC_STAGES = FFA_DEC_STAGES;
+constexpr int DEC_STAGES = 8;
 
 struct DecParams {
   const void* q;      // [R, Hq, D]
