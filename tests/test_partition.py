@@ -47,3 +47,29 @@ def test_lpt_partition():
         assert max(loads) <= sum(lens) / world + max(lens)
     with pytest.raises(ValueError):
         lpt_partition([1], 0)
+
+
+def test_e2e_chunks_cover_each_rank_once():
+    """bench.py's e2e pipeline: the chunks of a rank cover exactly its GQA
+    groups, with single-kv-head chunks at the ends."""
+    import bench
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            blocks = bench.rank_blocks(world, rank)
+            ch = bench.e2e_chunks(blocks, 4)
+            got = sorted((b, g) for b, g0, g1 in ch for g in range(g0, g1))
+            want = sorted((b, h) for b0, b1, h0, h1 in blocks for b in range(b0, b1) for h in range(h0, h1))
+            assert got == want
+            assert ch[0][2] - ch[0][1] == 1
+
+
+def test_kernel_head_dims():
+    from fastest_flash_attention_b200.attention import kernel_head_dims
+    assert kernel_head_dims(64, 64) == (64, 64)
+    assert kernel_head_dims(4, 4) == (64, 64)
+    assert kernel_head_dims(80, 80) == (128, 128)
+    assert kernel_head_dims(96, 64) == (128, 128)
+    assert kernel_head_dims(160, 128) == (192, 128)
+    assert kernel_head_dims(192, 128) == (192, 128)
+    assert kernel_head_dims(256, 256) is None
+    assert kernel_head_dims(64, 160) is None
