@@ -31,7 +31,16 @@ namespace ffa {
 constexpr int DEC_CHUNK = 16;     // tokens per chunk (one MMA K-step of P V)
 constexpr int DEC_CONSUMERS = 4;  // consumer warps
 constexpr int DEC_THREADS = (DEC_CONSUMERS + 1) * 32;
+// Stages of the K/V ring.  Consumer w takes chunks w, w + C, w + 2C, ... and
+// waits on stage idx % STAGES with parity (idx / STAGES) & 1.  With STAGES a
+// multiple of C the stage's previous chunk is the same warp's own, so the
+// barrier can never be two phases behind a waiting warp (where the parity
+// test would pass on the stale phase).  8 stages keep a CTA at 65 KB of smem:
+// three CTAs per SM (the register limit too), which measured 0.655 ms on
+// config 4 against 0.80 ms at 12 stages (two CTAs per SM) and 1.47 ms at 16
+// (one).
 constexpr int DEC_STAGES = 8;
+static_assert(DEC_STAGES % DEC_CONSUMERS == 0, "a stage's previous chunk must be the same consumer's");
 
 struct DecParams {
   const void* q;      // [R, Hq, D]
@@ -97,9 +106,12 @@ struct DecCfg {
   static constexpr int HALF = DEC_CHUNK * 128;           // 16 rows x 64 elements
   static constexpr int KV_BYTES = DEC_CHUNK * D * 2;     // one chunk of K (or V)
   static constexpr int STAGE = 2 * KV_BYTES;
-  static constexpr int MERGE_OFF = DEC_STAGES * STAGE;   // per-warp m, l, O for the CTA merge
+  // per-warp m, l, O for the CTA merge: over the stage ring, which is idle by
+  // then (a separate area would cost a third CTA per SM)
+  static constexpr int MERGE_OFF = 0;
   static constexpr int MERGE_BYTES = DEC_CONSUMERS * 16 * (D + 2) * 4;
-  static constexpr int BAR_OFF = MERGE_OFF + MERGE_BYTES;
+  static constexpr int RING = DEC_STAGES * STAGE;
+  static constexpr int BAR_OFF = RING > MERGE_BYTES ? RING : MERGE_BYTES;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
@@ -288,6 +300,11 @@ __global__ void __launch_bounds__(DEC_THREADS)
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
   }
+  // The merge area overlays the stage ring: every consumer must be done with
+  // its last chunk first.  After an abort, copies may still be landing in the
+  // ring (the producer drains them), so nothing is written.
+  asm volatile("bar.sync 1, %0;" ::"n"(DEC_CONSUMERS * 32) : "memory");
+  if (*abort_flag) return;
   float* wm = mrg + warp * 16 * (D + 2);  // per warp: 16 rows x (m, l, O[D])
   if (t == 0) {
     wm[g * (D + 2) + 0] = m_lo;
