@@ -299,6 +299,19 @@ def secondary_lines(dev, peaks, peak_src):
         "fwd_bwd_tflops": 3.5 * ff / (f_ms + b_ms) / 1e9,
         "frac_of_peak": 3.5 * ff / (f_ms + b_ms) / 1e9 / pk, "peak": f"{pk} TFLOP/s ({peak_src} bf16)"}
     del q, k, v, do, o, lse
+    # config 1 (the reference's CPU-runnable case): fp32 [2, 8, 1024, 64] causal fwd+bwd, computed
+    # in fp32 on the CUDA cores (no fp32 tensor-core operands); L2-resident (25 MB of inputs)
+    g = torch.Generator(device=dev).manual_seed(1)
+    q, k, v, do = (torch.randn(2, 8, 1024, 64, device=dev, generator=g) for _ in range(4))
+    o, lse = flash_fwd(q, k, v, scale=0.125, causal=True)
+    f1 = _time(lambda: flash_fwd(q, k, v, scale=0.125, causal=True), 20, dev)
+    b1 = _time(lambda: flash_bwd(do, q, k, v, o, lse, scale=0.125, causal=True), 20, dev)
+    ff1 = 4.0 * 64 * causal_pairs(1024) * 2 * 8
+    out["fp32_fwd_bwd_cfg1"] = {
+        "workload": "config 1: fp32 B=2 H=8 S=1024 D=64 causal, fp32 arithmetic (CUDA cores), L2-resident",
+        "fwd_ms": f1, "bwd_ms": b1, "fwd_tflops": ff1 / f1 / 1e9, "bwd_tflops": 2.5 * ff1 / b1 / 1e9,
+        "fwd_bwd_tflops": 3.5 * ff1 / (f1 + b1) / 1e9}
+    del q, k, v, do, o, lse
     # config 4: paged decode
     q, kp, vp, bt, lens, tot, mx = paged_decode_inputs(dev)
     d_ms = _time(lambda: paged_decode(q, kp, vp, bt, lens, max_ctx=mx), 20, dev)

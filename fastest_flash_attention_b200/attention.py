@@ -6,9 +6,11 @@ values.  The work is done by the sm_100a kernels in libffa_b200.so; there is
 no Triton path and no CPU fallback (CPU tensors raise).
 
 Numerics: fp16/bf16 inputs are consumed as-is by the tensor cores with fp32
-accumulation.  fp32 inputs are rounded to bf16 (or to ``compute_dtype`` when
-that is fp16/bf16) before the kernels run and the result is cast back to
-fp32, so fp32 callers get bf16-level accuracy.
+accumulation.  fp32 inputs are computed in fp32, as the reference does
+(kernels/cpu_reference.py:28-32 casts only when a lower ``compute_dtype`` is
+given): the fp32 kernels run on the CUDA cores, since the tensor cores take no
+fp32 operands.  With ``compute_dtype`` fp16/bf16, fp32 inputs are rounded to
+it and run on the tensor cores, and the result is cast back to fp32.
 """
 from __future__ import annotations
 
@@ -23,6 +25,8 @@ from .config import AttentionConfig
 from .utils import auto_select_block_size, maybe_unsqueeze_head
 
 _KERNEL_DTYPES = (torch.float16, torch.bfloat16)
+# dtype codes of ffa_fwd / ffa_bwd (FFA_DTYPE_*): fp32 selects the CUDA-core kernels
+_ATTN_DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 FWD_HEAD_DIMS = ((64, 64), (128, 128), (192, 128))  # kernel instantiations (qk, v)
 MAX_HEAD_DIM = 192  # qk head dim; v head dim up to 128
 
@@ -47,10 +51,15 @@ def _pad_last(t: torch.Tensor, width: int) -> torch.Tensor:
 
 
 def kernel_dtype(t: torch.Tensor, compute_dtype: Optional[torch.dtype] = None) -> torch.dtype:
+    """Dtype the kernels compute in: 16-bit inputs as they are; fp32 (and
+    fp64) inputs in fp32 unless ``compute_dtype`` asks for fp16/bf16 (tensor
+    cores); other input dtypes in bf16."""
     if t.dtype in _KERNEL_DTYPES:
         return t.dtype
     if compute_dtype in _KERNEL_DTYPES:
         return compute_dtype
+    if t.dtype in (torch.float32, torch.float64):
+        return torch.float32
     return torch.bfloat16
 
 
@@ -114,7 +123,7 @@ def flash_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float
     with torch.cuda.device(q.device):
         st = lib.ffa_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else None,
-            _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, Dv,
+            _ATTN_DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, Dv,
             _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o),
             float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0),
             bm_ptr, n_br, n_bc, int(mask_block[0]), int(mask_block[1]),
@@ -245,7 +254,7 @@ def flash_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     ws_bytes = lib.ffa_bwd_workspace_size(B, Hq, Sq)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     common = (dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-              dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, v.shape[3],
+              dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _ATTN_DTYPE_CODE[dt], B, Hq, Hkv, Sq, Skv, D, v.shape[3],
               _strides_bhs(q), _strides_bhs(k), _strides_bhs(v), _strides_bhs(o), _strides_bhs(dout),
               _strides_bhs(dq), _strides_bhs(dk), _strides_bhs(dv),
               float(scale), int(bool(causal)), int(q_offset), int(window or 0), float(softcap or 0.0))

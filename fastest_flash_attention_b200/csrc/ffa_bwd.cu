@@ -1168,9 +1168,14 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
     return FFA_ERR_INVALID_ARG;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0 || Hq % Hkv != 0) return FFA_ERR_INVALID_ARG;
   if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128))) return FFA_ERR_UNSUPPORTED;
-  if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
+  if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16 && dtype != FFA_DTYPE_F32) return FFA_ERR_UNSUPPORTED;
   const size_t need = ffa_bwd_workspace_size(B, Hq, Sq);
   if (!workspace || workspace_bytes < need) return FFA_ERR_WORKSPACE;
+  if (dtype == FFA_DTYPE_F32)
+    return f32_bwd(dout, q, k, v, o, lse, dq, dk, dv, B, Hq, Hkv, Sq, Skv, D, Dv, q_strides, k_strides, v_strides,
+                   o_strides, do_strides, dq_strides, dk_strides, dv_strides, scale, causal, q_offset, window,
+                   softcap, block_mask, n_br, n_bc, mask_bq, mask_bkv,
+                   reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 127) & ~uintptr_t(127)), stream);
   const int64_t* outs[3] = {dq_strides, dk_strides, dv_strides};
   for (auto* st : outs)
     if ((st[0] % 8) || (st[1] % 8) || (st[2] % 8)) return FFA_ERR_INVALID_ARG;

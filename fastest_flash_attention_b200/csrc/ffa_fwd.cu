@@ -617,11 +617,14 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides) return FFA_ERR_INVALID_ARG;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv < 0 || Hq % Hkv != 0) return FFA_ERR_INVALID_ARG;
   if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128))) return FFA_ERR_UNSUPPORTED;
-  if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16) return FFA_ERR_UNSUPPORTED;
+  if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16 && dtype != FFA_DTYPE_F32) return FFA_ERR_UNSUPPORTED;
   if (Skv > 65535 * FWD_BN) return FFA_ERR_UNSUPPORTED;
   if (block_mask && (n_br <= 0 || n_bc <= 0 || mask_bq <= 0 || mask_bkv <= 0 ||
                      (int64_t)n_br * mask_bq < Sq || (int64_t)n_bc * mask_bkv < Skv))
     return FFA_ERR_INVALID_ARG;
+  if (dtype == FFA_DTYPE_F32)
+    return f32_fwd(q, k, v, o, lse, B, Hq, Hkv, Sq, Skv, D, Dv, q_strides, k_strides, v_strides, o_strides, scale,
+                   causal, q_offset, window, softcap, block_mask, n_br, n_bc, mask_bq, mask_bkv, stream);
   if (!aligned16(o) || (o_strides[2] % 8) || (o_strides[1] % 8) || (o_strides[0] % 8)) return FFA_ERR_INVALID_ARG;
 
   FwdParams p{};

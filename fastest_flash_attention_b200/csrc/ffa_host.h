@@ -52,4 +52,18 @@ int smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// fp32 kernels on the CUDA cores (ffa_f32.cu), reached through ffa_fwd /
+// ffa_bwd / ffa_bwd_masked with dtype FFA_DTYPE_F32.
+int f32_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Sq,
+            int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+            const int64_t* o_strides, float scale, int causal, int q_offset, int window, float softcap,
+            const uint8_t* block_mask, int n_br, int n_bc, int mask_bq, int mask_bkv, void* stream);
+int f32_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+            void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int Sq, int Skv, int D, int Dv,
+            const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+            const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+            const int64_t* dk_strides, const int64_t* dv_strides, float scale, int causal, int q_offset,
+            int window, float softcap, const uint8_t* block_mask, int n_br, int n_bc, int mask_bq, int mask_bkv,
+            void* workspace, void* stream);
+
 }  // namespace ffa

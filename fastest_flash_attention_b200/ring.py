@@ -80,7 +80,9 @@ def _pair_visible(q0: int, lq: int, k0: int, lk: int, causal: bool, window: Opti
 
 def _kernel_attn(q, k, v, *, scale, causal, q_offset, window, softcap):
     from .attention import flash_fwd
-    return flash_fwd(q, k, v, scale=scale, causal=causal, q_offset=q_offset, window=window, softcap=softcap)
+    # the ring's partial merge takes 16-bit partials: fp32 pieces run on the tensor cores in bf16
+    return flash_fwd(q, k, v, scale=scale, causal=causal, q_offset=q_offset, window=window, softcap=softcap,
+                     compute_dtype=torch.bfloat16 if q.dtype == torch.float32 else None)
 
 
 def merge_partial(o_acc: torch.Tensor, lse_acc: torch.Tensor, o_part: torch.Tensor, lse_part: torch.Tensor) -> None:
@@ -215,7 +217,7 @@ def ring_attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
 def _kernel_bwd(dout, q, k, v, o, lse, *, scale, causal, q_offset, window, softcap):
     from .attention import flash_bwd
     return flash_bwd(dout, q, k, v, o, lse, scale=scale, causal=causal, q_offset=q_offset, window=window,
-                     softcap=softcap)
+                     softcap=softcap, compute_dtype=torch.bfloat16 if q.dtype == torch.float32 else None)
 
 
 def _split_seq(x: torch.Tensor, pieces) -> List[torch.Tensor]:

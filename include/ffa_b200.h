@@ -42,7 +42,8 @@ typedef enum {
   FFA_ERR_WORKSPACE = 5        /* workspace missing or too small */
 } ffa_status;
 
-/* F32 is accepted only where an entry point says so (the MLA projections). */
+/* F32 is accepted only where an entry point says so (ffa_fwd / ffa_bwd /
+ * ffa_bwd_masked, and the MLA projections). */
 typedef enum { FFA_DTYPE_F16 = 0, FFA_DTYPE_BF16 = 1, FFA_DTYPE_F32 = 2 } ffa_dtype;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -78,7 +79,10 @@ void ffa_set_wait_limit_ns(unsigned long long ns);
  * D is the query/key head dim, Dv the value (and output) head dim.
  * Supported (D, Dv): (64, 64), (128, 128), (192, 128) — the last is the MLA
  * prefill shape (modules/flash_mla.py:96-152: 128 + 64 rotary dims, values
- * not padded).  dtype f16/bf16.
+ * not padded).  dtype f16/bf16 (tensor cores), or f32: computed in fp32 on the
+ * CUDA cores (FFMA register tiles, fp32 accumulation), as the reference
+ * computes fp32 inputs (kernels/cpu_reference.py:28-32); q/k/v/o then need
+ * 16-byte aligned bases and strides that are multiples of 4 elements.
  * ------------------------------------------------------------------------- */
 int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B, int Hq,
             int Hkv, int Sq, int Skv, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
@@ -96,7 +100,8 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
  *   (GQA groups summed in order into dk / dv).  (D, Dv) in {(64, 64),
  *   (128, 128), (192, 128)}; the last is the MLA training shape.
  * Same mask / softcap semantics as ffa_fwd (no block mask: the reference
- * backward has none).  `workspace` must hold ffa_bwd_workspace_size() bytes
+ * backward has none).  dtype f32 runs the fp32 CUDA-core backward (same
+ * determinism; the workspace then holds Delta).  `workspace` must hold ffa_bwd_workspace_size() bytes
  * of device memory (padded base-2 LSE and Delta = rowsum(dO*O)).
  * Three kernel launches on `stream`: preprocess, dK/dV, dQ.
  * ------------------------------------------------------------------------- */

@@ -125,13 +125,14 @@ def test_config1_fp32_full():
     out = ffa().fastest_flash_attn_func(qc, kc, vc, causal=True, block_size=64)
     out.sum().backward()
     assert out.dtype == torch.float32 and qc.grad.dtype == torch.float32
-    qb, kb, vb = (t.to(torch.bfloat16).float().numpy() for t in (q, k, v))
-    ro, lse = O.flash_forward(qb, kb, vb, causal=True, return_lse=True)
-    assert np.abs(out.detach().cpu().numpy() - ro).max() <= 2e-2
-    rdq, rdk, rdv = O.flash_backward(np.ones_like(ro), qb, kb, vb, ro, lse, causal=True)
+    # fp32 inputs are computed in fp32 (CUDA-core kernels): the reference's fp32 tolerance
+    qn, kn, vn = (t.numpy() for t in (q, k, v))
+    ro, lse = O.flash_forward(qn, kn, vn, causal=True, return_lse=True)
+    assert np.abs(out.detach().cpu().numpy() - ro).max() <= 1e-5
+    rdq, rdk, rdv = O.flash_backward(np.ones_like(ro), qn, kn, vn, ro, lse, causal=True)
     for t, ref, nm in ((qc, rdq, "dq"), (kc, rdk, "dk"), (vc, rdv, "dv")):
         e = rel_err(t.grad, ref)
-        assert e <= G_TOL, f"{nm}: rel err {e:.3e}"
+        assert e <= 1e-4, f"{nm}: rel err {e:.3e}"
 
 
 def test_backward_deterministic_bitwise():
