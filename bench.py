@@ -546,17 +546,24 @@ def run_ours(args, world, rank, local):
             flash_fwd(q, k, v, scale=scale, causal=True)
 
     # ---- device-resident timing (value + roofline) ----
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    _lib.check_device_errors(dev)
+    # The clock sampler starts first and the warm-up steps run inside it, so
+    # the GPU goes from warm-up to the timed steps with no idle second in
+    # between (an idle GPU drops its clocks, and the first timed steps would
+    # pay the ramp).  A short device-side sleep after the barrier lets the host
+    # enqueue the timed steps ahead of the GPU, so the events measure the
+    # kernels and not the host's first launch.
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier(world)
-    torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        _lib.check_device_errors(dev)
+        barrier(world)
+        torch.cuda.synchronize(dev)
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(1_000_000)  # ~0.5 ms of device time, outside the timed region
         t0.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
