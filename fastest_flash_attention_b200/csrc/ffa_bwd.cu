@@ -63,7 +63,8 @@ struct BwdParams {
   float scale;         // softmax scale (applied to dK / dQ in the epilogue)
   float scale_log2;
   float sc_pre, sc_post;
-  float sc_small;      // |raw score| below which tanh_small is accurate (0.5 / sc_pre)
+  float sc_small;      // |raw score| below which softcap_small2 holds (0.5 / sc_pre)
+  float sc_poly[3];    // softcap_small2 coefficients for k = sc_pre
   int use_softcap;
   int causal, window;
   // optional tile mask [n_br, n_bc] of (mask_bq x mask_bkv) blocks, the one
@@ -139,7 +140,7 @@ __device__ __forceinline__ uint32_t block_mask_bits32(int x0, int bs, int nb, Ce
 // (COL_STATS, dK/dV kernel: cnl2 / cdl, 16-byte aligned) or are the row's
 // (rnl2 / rdl, dQ kernel).  With MASKED, columns c with (uint)(c - lo) >= cnt
 // are dropped, and with BITS also those whose bit c of `bits` is clear (the
-// block mask).  MODE 0: no softcap; 1: softcap with tanh by the series (FMA
+// block mask).  MODE 0: no softcap; 1: softcap with tanh by softcap_small2 (FMA
 // pipe); 2: softcap with tanh through ex2 / rcp.  Columns are processed in
 // pairs with packed fp32x2 instructions (per lane the same IEEE operations as
 // the scalar forms: dp - dl is computed as dp + dl * -1, and
@@ -172,8 +173,9 @@ __device__ __forceinline__ void bwd_chunk16(const BwdParams& p, const uint32_t* 
         x = ffma2(raw, f2(p.scale_log2), nl2[h]);
         g = ffma2(dl[h], f2(-1.f), dpv);
       } else if (MODE == 1) {
-        const float2 th = tanh_small2(fmul2(raw, f2(p.sc_pre)));
-        x = ffma2(th, f2(p.sc_post), nl2[h]);
+        const float2 y = softcap_small2(raw, p.sc_poly[0], p.sc_poly[1], p.sc_poly[2]);
+        x = ffma2(y, f2(p.scale_log2), nl2[h]);
+        const float2 th = fmul2(y, f2(p.sc_pre));
         g = fmul2(ffma2(dpv, f2(-1.f), dl[h]), ffma2(th, th, f2(-1.f)));
       } else {
         const float t0 = tanh_acc(raw.x * p.sc_pre), t1 = tanh_acc(raw.y * p.sc_pre);
@@ -206,7 +208,7 @@ __device__ __forceinline__ void bwd_chunk16_mode(const BwdParams& p, const uint3
     return;
   }
   // The cap is usually far above the scores, so tanh's argument is small:
-  // then the series on the FMA pipe is exact to fp32 and spares the MUFU.
+  // then the polynomial on the FMA pipe (error 2e-7) spares the MUFU.
   float mx = 0.f;
 #pragma unroll
   for (int c = 0; c < 16; c += 2) mx = fmax3(mx, fabsf(__uint_as_float(s[c])), fabsf(__uint_as_float(s[c + 1])));
@@ -1214,6 +1216,7 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
   p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
   p.sc_post = p.use_softcap ? softcap * 1.4426950408889634f : 0.f;
   p.sc_small = p.use_softcap ? 0.5f * softcap / scale : 0.f;
+  softcap_poly_coeffs(p.sc_pre, p.sc_poly);
   p.causal = causal;
   p.window = window > 0 ? window : 0;
   p.block_mask = block_mask;

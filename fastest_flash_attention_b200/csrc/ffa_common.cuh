@@ -376,28 +376,31 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
 }
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
-// tanh_small for two lanes with packed instructions; the same operations in
-// the same order per lane, so the results are bit-identical to tanh_small.
-__device__ __forceinline__ float2 tanh_small2(float2 x) {
-  const float2 x2 = fmul2(x, x);
-  float2 p = ffma2(f2(-8.8632e-3f), x2, f2(2.1869488536155203e-2f));
-  p = ffma2(p, x2, f2(-5.3968253968253971e-2f));
-  p = ffma2(p, x2, f2(1.3333333333333333e-1f));
-  p = ffma2(p, x2, f2(-3.3333333333333333e-1f));
-  return ffma2(fmul2(p, x2), x, x);
+// Softcap for small arguments.  With k = scale / softcap and |k s| <= 1/2,
+//   tanh(k s) = k y,   y = s (1 + r),   r = v (A + v (B + C v)),   v = s^2,
+// where (A, B, C) = (a k^2, b k^4, c k^6) and x (1 + a x^2 + b x^4 + c x^6)
+// is an odd degree-7 polynomial fitted to tanh on [-1/2, 1/2] (least squares
+// on Chebyshev nodes, reweighted towards minimax: max abs error 2.0e-7, 2.2e-7
+// evaluated in fp32).  softcap * log2(e) * tanh(k s) = scale * log2(e) * y, so
+// callers use y with the plain score multiplier.  Two lanes per packed
+// instruction: five FMA-pipe instructions per pair of scores.
+constexpr double SOFTCAP_POLY_A = -0.3332648070862027;
+constexpr double SOFTCAP_POLY_B = 0.13186077719149775;
+constexpr double SOFTCAP_POLY_C = -0.04423483979939102;
+
+// (A, B, C) for k = scale / softcap (host side, in double, then rounded).
+inline void softcap_poly_coeffs(float k, float* abc) {
+  const double k2 = (double)k * (double)k;
+  abc[0] = (float)(SOFTCAP_POLY_A * k2);
+  abc[1] = (float)(SOFTCAP_POLY_B * k2 * k2);
+  abc[2] = (float)(SOFTCAP_POLY_C * k2 * k2 * k2);
 }
 
-// tanh on |x| <= 1/2 by its Taylor series to x^11 (odd terms; coefficients
-// 1, -1/3, 2/15, -17/315, 62/2835, -1382/155925).  The first omitted term
-// bounds the error: 21844/6081075 * 2^-13 < 4.4e-7.  FMA pipe only.
-__device__ __forceinline__ float tanh_small(float x) {
-  const float x2 = x * x;
-  float p = -8.8632e-3f;                    // -1382/155925
-  p = fmaf(p, x2, 2.1869488536155203e-2f);  //  62/2835
-  p = fmaf(p, x2, -5.3968253968253971e-2f); // -17/315
-  p = fmaf(p, x2, 1.3333333333333333e-1f);  //  2/15
-  p = fmaf(p, x2, -3.3333333333333333e-1f); // -1/3
-  return fmaf(p * x2, x, x);
+__device__ __forceinline__ float2 softcap_small2(float2 s, float a, float b, float c) {
+  const float2 v = fmul2(s, s);
+  float2 t = ffma2(f2(c), v, f2(b));
+  t = ffma2(t, v, f2(a));
+  return ffma2(s, fmul2(t, v), s);
 }
 
 template <typename T>

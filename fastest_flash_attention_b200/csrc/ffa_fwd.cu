@@ -92,6 +92,7 @@ struct FwdParams {
   float scale_log2;   // scale * log2(e)
   float sc_pre;       // scale / softcap
   float sc_post;      // softcap * log2(e)
+  float sc_poly[3];   // softcap_small2 coefficients for k = sc_pre
   int use_softcap;
   int causal, window;
   const uint8_t* block_mask;
@@ -388,9 +389,11 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
       // softcap, tanh(s*scale/softcap) computed in place (mul = softcap*log2 e).
       float mul = p.scale_log2;
       if (p.use_softcap) {
-        // tanh(s*scale/softcap): the FMA-pipe series when every argument of
-        // the warp's tile is within 1/2 (the usual case, softcap >> scores),
-        // else the exact exp-based form (two MUFU ops per score).
+        // tanh(s*scale/softcap): the FMA-pipe polynomial when every argument
+        // of the warp's tile is within 1/2 (the usual case, softcap >> scores;
+        // s becomes y with tanh = k y, and the exponent keeps mul =
+        // scale*log2 e), else the exact exp-based form (two MUFU ops per
+        // score, mul = softcap*log2 e).
         float amax = 0.f;
 #pragma unroll
         for (int c = 0; c < FWD_BN; c += 2)
@@ -399,17 +402,17 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
           // pairs with packed instructions (per lane the same operations)
 #pragma unroll
           for (int c = 0; c < FWD_BN; c += 2) {
-            const float2 th = tanh_small2(
-                fmul2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), f2(p.sc_pre)));
-            s[c] = __float_as_uint(th.x);
-            s[c + 1] = __float_as_uint(th.y);
+            const float2 y = softcap_small2(make_float2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])),
+                                            p.sc_poly[0], p.sc_poly[1], p.sc_poly[2]);
+            s[c] = __float_as_uint(y.x);
+            s[c + 1] = __float_as_uint(y.y);
           }
         } else {
 #pragma unroll
           for (int c = 0; c < FWD_BN; ++c)
             s[c] = __float_as_uint(tanh_acc(__uint_as_float(s[c]) * p.sc_pre));
+          mul = p.sc_post;  // softcap*log2(e) > 0: applied in the exponent's FMA
         }
-        mul = p.sc_post;  // softcap*log2(e) > 0: applied in the exponent's FMA
       }
       const int c0 = j * FWD_BN;
       const bool need_mask = (p.causal && c0 + FWD_BN - 1 > a_lo) ||
@@ -645,6 +648,7 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   p.use_softcap = softcap > 0.f;
   p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
   p.sc_post = p.use_softcap ? softcap * 1.4426950408889634f : 0.f;
+  softcap_poly_coeffs(p.sc_pre, p.sc_poly);
   p.causal = causal;
   p.window = window > 0 ? window : 0;
   p.block_mask = block_mask;
