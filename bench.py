@@ -378,6 +378,21 @@ def secondary_lines(dev, peaks, peak_src):
         "workload": "MLADecoder.step, 16 requests, context 4096 -> 4116, hidden 4096, 32 heads, latent 512 + rope 64, "
                     "bf16 weights N(0, 0.02)", "ms_per_step": st_ms, "tokens_per_s": R / st_ms * 1e3,
         "timing": "CUDA events around 20 consecutive steps, host work included (the cache grows by a token per step)"}
+    # the same step replayed from a CUDA graph (MLADecoder.step_graphed): one
+    # pinned metadata copy, one input copy and one graph launch per step
+    for _ in range(3):
+        dec.step_graphed(x, list(range(R)))
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(n_steps):
+        dec.step_graphed(x, list(range(R)))
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sg_ms = e0.elapsed_time(e1) / n_steps
+    out["mla_decode_step_graphed_cfg5"] = {
+        "workload": "MLADecoder.step_graphed, same model and cache as mla_decode_step_cfg5 (context 4119 -> 4142)",
+        "ms_per_step": sg_ms, "tokens_per_s": R / sg_ms * 1e3,
+        "timing": "CUDA events around 20 consecutive steps, host work included (allocator, metadata copy, replay)"}
     del dec, mod
     return out
 

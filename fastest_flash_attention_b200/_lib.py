@@ -192,7 +192,12 @@ _DATA_ERRORS = {
 
 
 def sync_check_enabled() -> bool:
-    return os.environ.get("FFA_SYNC_CHECK", "0") not in ("", "0")
+    """FFA_SYNC_CHECK=1: synchronise after each call and read the error word
+    (never while a CUDA graph is being captured, where a synchronisation is
+    not allowed; a replayed graph is checked by the caller)."""
+    if os.environ.get("FFA_SYNC_CHECK", "0") in ("", "0"):
+        return False
+    return not torch.cuda.is_current_stream_capturing()
 
 
 def check_device_errors(device: torch.device | None = None) -> None:

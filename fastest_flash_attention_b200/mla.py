@@ -23,6 +23,7 @@ from __future__ import annotations
 import math
 from typing import List, Optional, Sequence
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -185,6 +186,58 @@ class MLADecoder:
                                  slots)
         return self.mla(x)
 
+    def _append_rows(self, lat: torch.Tensor, kr: torch.Tensor, pos_t: torch.Tensor, slot_t: torch.Tensor) -> None:
+        """_append_latents with positions and slots already in device int32 tensors."""
+        rows = self.cache.pages.view(-1, self.cache.pages.shape[-1])
+        lib = _lib.load()
+        with torch.cuda.device(rows.device):
+            st = lib.ffa_mla_latent_append(lat.data_ptr(), lat.stride(0), kr.data_ptr(), kr.stride(0),
+                                           pos_t.data_ptr(), slot_t.data_ptr(), self._inv_freq().data_ptr(),
+                                           rows.data_ptr(), rows.shape[0], _lib.IN_DTYPE_CODE[lat.dtype],
+                                           _lib.DTYPE_CODE[rows.dtype], lat.shape[0], lat.shape[1], kr.shape[1],
+                                           _lib.stream_of(rows))
+        _lib.check(st, "ffa_mla_latent_append")
+
+    def _device_step(self, x2d: torch.Tensor, pos_t: torch.Tensor, slot_t: torch.Tensor, bt: torch.Tensor,
+                     lens: torch.Tensor, max_ctx: int) -> torch.Tensor:
+        """The device work of one decode step, x2d [R, hidden] -> [R, hidden],
+        given the new tokens' positions and cache slots, the block table and
+        the context lengths (device int32).  No host synchronisation and no
+        host-to-device copy, so it can be captured in a CUDA graph."""
+        m = self.mla
+        R = x2d.shape[0]
+        H, d, r, L = m.num_heads, m.head_dim, m.rope_dim, m.latent_dim
+        y = x2d @ self._weights().t()                          # [R, H d + H r + L + r]
+        q_nope = y[:, :H * d].view(R, H, d)
+        q_rope = y[:, H * d:H * (d + r)].view(R, H, r)
+        lat = y[:, H * (d + r):H * (d + r) + L]
+        kr = y[:, H * (d + r) + L:]
+        self._append_rows(lat, kr, pos_t, slot_t)
+        w_uk, w_uv = absorbed_weights(m)
+        if w_uk.dtype != y.dtype:
+            raise ValueError("MLA decode needs activations and weights of one dtype")
+        lib = _lib.load()
+        dev = x2d.device
+        q = torch.empty((R, H, L + r), dtype=self.dtype, device=dev)
+        in_code = _lib.IN_DTYPE_CODE[y.dtype]
+        with torch.cuda.device(dev):
+            st = lib.ffa_mla_q_absorb(q_nope.data_ptr(), _lib.i64arr(q_nope.stride(0), q_nope.stride(1)),
+                                      q_rope.data_ptr(), _lib.i64arr(q_rope.stride(0), q_rope.stride(1)),
+                                      w_uk.data_ptr(), _lib.i64arr(w_uk.stride(0), w_uk.stride(1)),
+                                      pos_t.data_ptr(), self._inv_freq().data_ptr(), q.data_ptr(),
+                                      _lib.i64arr(q.stride(0), q.stride(1)), in_code, _lib.DTYPE_CODE[self.dtype],
+                                      R, H, d, L, r, _lib.stream_of(q))
+        _lib.check(st, "ffa_mla_q_absorb")
+        o_lat = mla_decode(q, self.cache.pages, bt, lens, scale=m.scale, max_ctx=max_ctx)
+        o = torch.empty((R, H * (d + r)), dtype=y.dtype, device=dev)
+        with torch.cuda.device(dev):
+            st = lib.ffa_mla_o_absorb(o_lat.data_ptr(), _lib.i64arr(o_lat.stride(0), o_lat.stride(1)),
+                                      w_uv.data_ptr(), _lib.i64arr(w_uv.stride(0), w_uv.stride(1)), o.data_ptr(),
+                                      o.stride(0), in_code, _lib.DTYPE_CODE[o_lat.dtype], R, H, d, L, r,
+                                      _lib.stream_of(o))
+        _lib.check(st, "ffa_mla_o_absorb")
+        return m.o_proj(o)
+
     @torch.no_grad()
     def step(self, x: torch.Tensor, seq_ids: Sequence[int]) -> torch.Tensor:
         """One new token per sequence: x [R, 1, hidden] -> [R, 1, hidden].
@@ -194,40 +247,114 @@ class MLADecoder:
         paged latent decode) and one more (value absorption into o_proj's
         input rows) before the o_proj GEMM.  No per-request Python loop runs
         on the device path."""
-        m = self.mla
         R = x.shape[0]
-        H, d, r, L = m.num_heads, m.head_dim, m.rope_dim, m.latent_dim
+        dev = x.device
         pos = [self.cache.sequences.get(s, {"len": 0})["len"] for s in seq_ids]
         slots = [self.cache._slots(s, 1)[0] for s in seq_ids]
-        y = x[:, 0] @ self._weights().t()                      # [R, H d + H r + L + r]
-        q_nope = y[:, :H * d].view(R, H, d)
-        q_rope = y[:, H * d:H * (d + r)].view(R, H, r)
-        lat = y[:, H * (d + r):H * (d + r) + L]
-        kr = y[:, H * (d + r) + L:]
-        self._append_latents(lat, kr, pos, slots)
-        w_uk, w_uv = absorbed_weights(m)
-        lib = _lib.load()
-        dev = x.device
         pos_t = torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True)
-        q = torch.empty((R, H, L + r), dtype=self.dtype, device=dev)
-        in_code = _lib.IN_DTYPE_CODE[y.dtype]
-        if w_uk.dtype != y.dtype:
-            raise ValueError("MLA decode needs activations and weights of one dtype")
-        with torch.cuda.device(dev):
-            st = lib.ffa_mla_q_absorb(q_nope.data_ptr(), _lib.i64arr(q_nope.stride(0), q_nope.stride(1)),
-                                      q_rope.data_ptr(), _lib.i64arr(q_rope.stride(0), q_rope.stride(1)),
-                                      w_uk.data_ptr(), _lib.i64arr(w_uk.stride(0), w_uk.stride(1)),
-                                      pos_t.data_ptr(), self._inv_freq().data_ptr(), q.data_ptr(),
-                                      _lib.i64arr(q.stride(0), q.stride(1)), in_code, _lib.DTYPE_CODE[self.dtype],
-                                      R, H, d, L, r, _lib.stream_of(q))
-        _lib.check(st, "ffa_mla_q_absorb")
+        slot_t = torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True)
         bt, lens = self.cache.block_table(seq_ids)
-        o_lat = mla_decode(q, self.cache.pages, bt, lens, scale=m.scale, max_ctx=max(pos) + 1)
-        o = torch.empty((R, H * (d + r)), dtype=y.dtype, device=dev)
-        with torch.cuda.device(dev):
-            st = lib.ffa_mla_o_absorb(o_lat.data_ptr(), _lib.i64arr(o_lat.stride(0), o_lat.stride(1)),
-                                      w_uv.data_ptr(), _lib.i64arr(w_uv.stride(0), w_uv.stride(1)), o.data_ptr(),
-                                      o.stride(0), in_code, _lib.DTYPE_CODE[o_lat.dtype], R, H, d, L, r,
-                                      _lib.stream_of(o))
-        _lib.check(st, "ffa_mla_o_absorb")
-        return m.o_proj(o).view(R, 1, -1)
+        return self._device_step(x[:, 0], pos_t, slot_t, bt, lens, max(pos) + 1).view(R, 1, -1)
+
+    @torch.no_grad()
+    def step_graphed(self, x: torch.Tensor, seq_ids: Sequence[int]) -> torch.Tensor:
+        """step() replayed from a CUDA graph: the same launches, captured once
+        per (number of sequences, context bucket) and replayed, so a step
+        costs the host one small copy and one graph launch instead of a dozen
+        kernel launches and their argument set-up.
+
+        Contexts are bucketed to multiples of 1024 tokens: the block table is
+        padded to the bucket's page count and the decode grid covers the
+        bucket (splits past a sequence's length do no work); the split size
+        is chosen for the bucket, as step() chooses it for the longest
+        context.  The
+        host keeps the page allocator (FIFO, as in step()); each step's
+        positions, slots, context lengths and block table travel in one
+        pinned int32 buffer.  A graph is recaptured when the stacked input
+        weights change.  The result is a new tensor (the graph's output buffer
+        is reused by the next replay)."""
+        R = x.shape[0]
+        dev = x.device
+        ps = self.cache.page_size
+        pos = [self.cache.sequences.get(s, {"len": 0})["len"] for s in seq_ids]
+        slots = [self.cache._slots(s, 1)[0] for s in seq_ids]
+        ctx_max = max(pos) + 1
+        bucket = -(-ctx_max // 1024) * 1024
+        W = -(-bucket // ps)
+        key = (R, bucket, x.dtype, self._weights().data_ptr())
+        graphs = self.__dict__.setdefault("_graphs", {})
+        gr = graphs.get(key)
+        if gr is None:
+            gr = _StepGraph(R, W, x.shape[-1], x.dtype, dev)
+        meta = gr.next_host_meta()
+        mv = meta.numpy()  # [pos | slots | lens | block table (R x W)], filled in place
+        mv[:R] = pos
+        mv[R:2 * R] = slots
+        bt = mv[3 * R:].reshape(R, W)
+        rows = gr.host_rows()  # (sequence, pages) each row of this staging buffer holds
+        n_pages = self.cache.pages.shape[0]
+        for i, s in enumerate(seq_ids):
+            seq = self.cache.sequences[s]
+            t = seq["page_table"]
+            if seq["len"] > W * ps:
+                raise ValueError(f"sequence {s}: context {seq['len']} exceeds the block table ({W} pages)")
+            mv[2 * R + i] = seq["len"]
+            if rows[i] != (s, len(t)):  # rewrite a row only when its table grew or changed hands
+                row = np.asarray(t, dtype=np.int32)
+                # the allocator's own pages; checked all the same, as the decode kernels rely on them
+                if row.size and (int(row.min()) < 0 or int(row.max()) >= n_pages):
+                    raise ValueError(f"sequence {s}: a page id is outside [0, {n_pages})")
+                bt[i, :row.size] = row
+                bt[i, row.size:] = 0
+                rows[i] = (s, len(t))
+        gr.meta.copy_(meta, non_blocking=True)
+        gr.record_host_meta_use()
+        gr.x.copy_(x[:, 0])
+        if key not in graphs:
+            gr.capture(lambda: self._device_step(gr.x, gr.meta[:R], gr.meta[R:2 * R], gr.meta[3 * R:].view(R, W),
+                                                 gr.meta[2 * R:3 * R], bucket))
+            graphs[key] = gr
+        gr.graph.replay()
+        return gr.out.clone().view(R, 1, -1)
+
+
+class _StepGraph:
+    """Static buffers and the captured graph of one MLADecoder.step_graphed shape."""
+
+    def __init__(self, R: int, W: int, hidden: int, dtype: torch.dtype, dev: torch.device):
+        self.x = torch.empty((R, hidden), dtype=dtype, device=dev)
+        self.meta = torch.empty(3 * R + R * W, dtype=torch.int32, device=dev)
+        # two pinned staging buffers, used in turn; an event marks when the
+        # copy out of each has run, so it is not overwritten before then
+        self._host = [torch.zeros(self.meta.numel(), dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._rows = [[None] * R, [None] * R]
+        self._events = [None, None]
+        self._turn = 0
+        self.graph = None
+        self.out = None
+
+    def next_host_meta(self) -> torch.Tensor:
+        self._turn ^= 1
+        ev = self._events[self._turn]
+        if ev is not None:
+            ev.synchronize()
+        return self._host[self._turn]
+
+    def host_rows(self) -> list:
+        return self._rows[self._turn]
+
+    def record_host_meta_use(self) -> None:
+        ev = torch.cuda.Event()
+        ev.record()
+        self._events[self._turn] = ev
+
+    def capture(self, body) -> None:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # warm-up launches (idempotent: same rows, same slots)
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = body()

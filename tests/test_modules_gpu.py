@@ -237,3 +237,29 @@ def test_mla_projection_kernels_vs_torch(wdtype):
     assert rel(rows[slots], ref_rows.detach().cpu().numpy()) <= 1e-2
     untouched = [i for i in range(rows.shape[0]) if i not in slots]
     assert not rows[untouched].any()
+
+
+def test_mla_graphed_step_matches_step():
+    """MLADecoder.step_graphed (the step captured in CUDA graphs, per context
+    bucket) against the eager step on ragged contexts, across a bucket change
+    (1024 -> 2048 tokens, which captures a second graph)."""
+    m = ffa()
+    torch.manual_seed(6)
+    mod = m.FastestFlashMLA(hidden_size=512, num_heads=32, head_dim=128, latent_dim=512, rope_dim=64).cuda().eval()
+    for prm in mod.parameters():
+        torch.nn.init.normal_(prm, std=0.02)
+    eager = m.MLADecoder(mod, max_pages=200, page_size=16)
+    graphed = m.MLADecoder(mod, max_pages=200, page_size=16)
+    p0 = torch.randn(1, 1015, 512, device="cuda")
+    p1 = torch.randn(1, 333, 512, device="cuda")
+    for dec in (eager, graphed):
+        dec.prefill(p0, [0])
+        dec.prefill(p1, [1])
+    for _ in range(14):  # sequence 0 goes from 1015 to 1029 tokens
+        xs = torch.randn(2, 1, 512, device="cuda")
+        y_e = eager.step(xs, [0, 1])
+        y_g = graphed.step_graphed(xs, [0, 1])
+        assert y_g.shape == y_e.shape
+        assert rel(y_g, y_e.float().cpu().numpy()) <= 1e-2
+    assert len(graphed._graphs) == 2
+    assert torch.equal(graphed.cache.pages, eager.cache.pages)
