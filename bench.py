@@ -715,6 +715,12 @@ def run_profile(args):
         o, lse = flash_fwd(q, k, v, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
         for _ in range(n):
             flash_bwd(do, q, k, v, o, lse, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
+    elif args.profile == "fp32":
+        # config 1: fp32 [2, 8, 1024, 64] causal forward + backward (CUDA-core kernels)
+        q, k, v, do = (torch.randn(2, 8, 1024, 64, device=dev) for _ in range(4))
+        for _ in range(n):
+            o, lse = flash_fwd(q, k, v, scale=0.125, causal=True)
+            flash_bwd(do, q, k, v, o, lse, scale=0.125, causal=True)
     elif args.profile == "decode":
         q, kp, vp, bt, lens, tot, mx = paged_decode_inputs(dev)
         for _ in range(n):
@@ -739,7 +745,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["full", "small"], default="full")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
-    ap.add_argument("--profile", choices=["bwd", "decode", "mla"], default=None,
+    ap.add_argument("--profile", choices=["bwd", "decode", "mla", "fp32"], default=None,
                     help="run only that kernel family a few times on a capture-sized case (for ncu)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the other kernels' lines")
     args = ap.parse_args()
