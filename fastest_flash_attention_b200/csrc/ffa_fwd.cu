@@ -74,13 +74,26 @@ template <int D, int DV, int NQT = 2>
 struct FwdCfg {
   static constexpr int TILE = FWD_BM * D * 2;     // one 128-row Q (or K) tile
   static constexpr int VTILE = FWD_BN * DV * 2;   // one 128-row V tile
-  static constexpr int BUF = TILE > VTILE ? TILE : VTILE;  // ring slot (holds a K or a V tile)
+  // D <= 128: one ring of NBUF equal slots, K and V of each key tile in turn,
+  // fed by one producer warp.  D = 192: the two Q tiles take 96 KB, which
+  // leaves room for one K and one V slot of a shared ring; instead K and V
+  // get rings of their own (two 48 KB K slots, one 32 KB V slot), each fed by
+  // its own producer warp, so the next-but-one K tile loads a whole key tile
+  // ahead (config 5 prefill 3.61 -> 3.26 ms).
+  static constexpr bool SPLIT = NQT == 2 && D == 192;
+  static constexpr int BUF = TILE > VTILE ? TILE : VTILE;  // shared-ring slot (holds a K or a V tile)
   static constexpr int NBUF = NQT == 2 ? ((D == 64) ? 8 : (D == 128 ? 4 : 2)) : (D == 64 ? 4 : 2);
+  static constexpr int NK = 2, NV = 1;  // SPLIT: K slots (barriers [0, NK)), V slots (barriers [4, 4 + NV))
+  // key tiles recorded per CTA when a block mask filters them (D = 192: what
+  // the shared memory left over holds)
+  static constexpr int MAX_LIST = SPLIT ? 512 : FWD_MAX_LIST;
   static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = NQT * TILE;
-  static constexpr int BAR_OFF = KV_OFF + NBUF * BUF;
+  static constexpr int KV_OFF = NQT * TILE;                           // shared ring, or the K ring
+  static constexpr int V_OFF = SPLIT ? KV_OFF + NK * TILE : KV_OFF;   // the V ring
+  static constexpr int BAR_OFF = SPLIT ? V_OFF + NV * VTILE : KV_OFF + NBUF * BUF;
   static constexpr int LIST_OFF = BAR_OFF + 512;
-  static constexpr int SMEM = LIST_OFF + FWD_MAX_LIST * 2 + 1024;  // + alignment slack
+  static constexpr int SMEM = LIST_OFF + MAX_LIST * 2 + 1024;  // + alignment slack
+  static_assert(SMEM <= 227 * 1024, "forward shared memory budget");
 };
 
 struct FwdParams {
@@ -140,6 +153,7 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Cfg::Q_OFF;
   uint8_t* sKV = smem + Cfg::KV_OFF;
+  uint8_t* sV = smem + Cfg::V_OFF;
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + Cfg::BAR_OFF);
   uint16_t* list = reinterpret_cast<uint16_t*>(smem + Cfg::LIST_OFF);
   volatile int* abort_flag = &bars->abort;
@@ -171,7 +185,7 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
       mbar_init(&bars->o_done[t], 1);
     }
     mbar_init(&bars->drain, 1);
-    for (int i = 0; i < Cfg::NBUF; ++i) {
+    for (int i = 0; i < 8; ++i) {  // shared ring [0, NBUF); split rings: K [0, NK), V [4, 4 + NV)
       mbar_init(&bars->kv_full[i], 1);
       mbar_init(&bars->kv_empty[i], 1);
     }
@@ -213,14 +227,14 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
         }
         const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
         const int pos = count + __popc(ballot & ((1u << lane) - 1u));
-        if (keep && pos < FWD_MAX_LIST) list[pos] = (uint16_t)j;
+        if (keep && pos < Cfg::MAX_LIST) list[pos] = (uint16_t)j;
         count += __popc(ballot);
       }
       if (lane == 0) {
         bars->j_lo = 0;
-        bars->n_tiles = min(count, FWD_MAX_LIST);
+        bars->n_tiles = min(count, Cfg::MAX_LIST);
         bars->use_list = 1;
-        if (count > FWD_MAX_LIST && p.ec.err) atomicCAS(p.ec.err, 0u, 0x1FFu);
+        if (count > Cfg::MAX_LIST && p.ec.err) atomicCAS(p.ec.err, 0u, 0x1FFu);
       }
     }
   }
@@ -237,7 +251,49 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
 
   if (warp >= 4 * NQT) {
    regs_dec<Shape::REGS_OTHER>();
-   if (warp == FWD_WARP_LOAD) {
+   if (Cfg::SPLIT && (warp == FWD_WARP_LOAD || warp == FWD_WARP_LOAD + 2)) {
+    // --------------------------- split-ring producers -----------------------
+    // warp FWD_WARP_LOAD: Q, then the K ring; warp FWD_WARP_LOAD + 2: the V ring.
+    if (lane == 0) {
+      const bool is_v = warp != FWD_WARP_LOAD;
+      const CUtensorMap* tm = is_v ? &tmV : &tmK;
+      tma_prefetch_desc(tm);
+      const uint64_t pol_kv = policy_evict_last();
+      if (!is_v) {
+        tma_prefetch_desc(&tmQ);
+        const uint64_t pol_q = policy_evict_first();
+        mbar_arrive_expect_tx(&bars->q_full, FWD_NQT * Cfg::TILE);
+        for (int t = 0; t < FWD_NQT; ++t)
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(&tmQ, &bars->q_full, sQ + t * Cfg::TILE + c * (FWD_BM * 128), c * 64, q_lo + t * FWD_BM,
+                        h, b, pol_q);
+      }
+      const int nslot = is_v ? Cfg::NV : Cfg::NK;
+      const int bar0 = is_v ? 4 : 0;
+      const int bytes = is_v ? Cfg::VTILE : Cfg::TILE;
+      uint8_t* ring = is_v ? sV : sKV;
+      int issued = 0;  // slots armed so far
+      for (int it = 0; it < n; ++it) {
+        const int j = tile_at(it);
+        const int buf = it % nslot, use = it / nslot;
+        if (use > 0 &&
+            !mbar_wait(&bars->kv_empty[bar0 + buf], (use - 1) & 1, p.ec, abort_flag, SITE_FWD_KV_EMPTY))
+          break;
+        mbar_arrive_expect_tx(&bars->kv_full[bar0 + buf], bytes);
+        ++issued;
+        uint8_t* dst = ring + buf * bytes;
+        for (int c = 0; c < (is_v ? DV : D) / 64; ++c)
+          tma_load_4d(tm, &bars->kv_full[bar0 + buf], dst + c * (FWD_BN * 128), c * 64, j * FWD_BN, hkv, b, pol_kv);
+      }
+      if (*abort_flag) {
+        // Let copies still in flight land before the CTA gives up its smem.
+        if (!is_v) mbar_wait(&bars->q_full, 0, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+        for (int s = max(0, issued - nslot); s < issued; ++s)
+          mbar_wait(&bars->kv_full[bar0 + s % nslot], (s / nslot) & 1, p.ec, abort_flag, SITE_FWD_DRAIN, true);
+      }
+    }
+    __syncwarp();
+   } else if (!Cfg::SPLIT && warp == FWD_WARP_LOAD) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -289,11 +345,12 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
       // thread's instruction count (and so its issue-slot needs) minimal.
       const uint64_t q_base = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t k_base = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
-      const uint64_t v_base = make_sdesc_sw128(smem_u32(sKV), FWD_BN * 128, 1024);
+      const uint64_t v_base = make_sdesc_sw128(smem_u32(sV), FWD_BN * 128, 1024);
+      constexpr int KSLOT = Cfg::SPLIT ? Cfg::TILE : Cfg::BUF, VSLOT = Cfg::SPLIT ? Cfg::VTILE : Cfg::BUF;
       auto issue_qk = [&](int t, int buf) {
         const uint32_t d = tmem + t * 128;
         const uint64_t qa = q_base + (uint64_t)((t * Cfg::TILE) >> 4);
-        const uint64_t kb = k_base + (uint64_t)((buf * Cfg::BUF) >> 4);
+        const uint64_t kb = k_base + (uint64_t)((buf * KSLOT) >> 4);
         // Fully unrolled at D <= 128; at D = 192 a full unroll of the 12 k-steps
         // made the issuing warp spill (184-byte stack frame) and ran ~2 % slower.
 #pragma unroll(D > 128 ? 4 : D / 16)
@@ -307,7 +364,7 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
       auto issue_pv = [&](int t, int buf, bool acc, int chunk) {
         const uint32_t d = tmem + O_COL + t * 128;
         const uint32_t a = tmem + t * 128;
-        const uint64_t vb = v_base + (uint64_t)((buf * Cfg::BUF) >> 4);
+        const uint64_t vb = v_base + (uint64_t)((buf * VSLOT) >> 4);
         constexpr int KS_PER = FWD_BN / 16 / FWD_PCH;
 #pragma unroll
         for (int kk = 0; kk < KS_PER; ++kk) {
@@ -328,10 +385,20 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
         }
       }
       for (int it = 0; it < n && ok; ++it) {
-        const int vs = 2 * it + 1, vb = vs % Cfg::NBUF;
+        // slot (vb: V of tile it, kb: K of tile it + 1), its barrier and phase
+        int vb, kb, vbar, kbar;
+        uint32_t vph, kph;
+        if constexpr (Cfg::SPLIT) {
+          vb = it % Cfg::NV, kb = (it + 1) % Cfg::NK;
+          vbar = 4 + vb, kbar = kb;
+          vph = (it / Cfg::NV) & 1, kph = ((it + 1) / Cfg::NK) & 1;
+        } else {
+          const int vs = 2 * it + 1, ks_ = 2 * (it + 1);
+          vb = vbar = vs % Cfg::NBUF, kb = kbar = ks_ % Cfg::NBUF;
+          vph = (vs / Cfg::NBUF) & 1, kph = (ks_ / Cfg::NBUF) & 1;
+        }
         const bool has_next = it + 1 < n;
-        const int ks_ = 2 * (it + 1), kb = ks_ % Cfg::NBUF;
-        if (!mbar_wait_mma(&bars->kv_full[vb], (vs / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
+        if (!mbar_wait_mma(&bars->kv_full[vbar], vph, p.ec, abort_flag, SITE_FWD_KV_FULL)) break;
         for (int t = 0; t < FWD_NQT && ok; ++t) {
           for (int k = 0; k < FWD_PCH; ++k) {
             if (!mbar_wait_mma(&bars->p_full[t][k], it & 1, p.ec, abort_flag, SITE_FWD_P_FULL)) {
@@ -343,8 +410,12 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
           }
           if (!ok) break;
           mma_commit(&bars->o_done[t]);
+          // With two slots or a V ring of one, V of tile it is released as soon
+          // as the last query tile's P·V retires (before the next S), so its
+          // refill starts earlier; deeper shared rings release it below.
+          if ((Cfg::SPLIT || Cfg::NBUF == 2) && t == FWD_NQT - 1) mma_commit(&bars->kv_empty[vbar]);
           if (has_next) {
-            if (t == 0 && !mbar_wait_mma(&bars->kv_full[kb], (ks_ / Cfg::NBUF) & 1, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
+            if (t == 0 && !mbar_wait_mma(&bars->kv_full[kbar], kph, p.ec, abort_flag, SITE_FWD_KV_FULL)) {
               ok = false;
               break;
             }
@@ -354,8 +425,8 @@ __global__ void __launch_bounds__(FwdShape<NQT>::THREADS, FwdShape<NQT>::MIN_BLO
           }
         }
         if (!ok) break;
-        mma_commit(&bars->kv_empty[vb]);
-        if (has_next) mma_commit(&bars->kv_empty[kb]);
+        if (!(Cfg::SPLIT || Cfg::NBUF == 2)) mma_commit(&bars->kv_empty[vbar]);
+        if (has_next) mma_commit(&bars->kv_empty[kbar]);
       }
       // Every MMA must retire before TMEM is released.
       mma_commit(&bars->drain);
@@ -622,6 +693,8 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 192 && Dv == 128))) return FFA_ERR_UNSUPPORTED;
   if (dtype != FFA_DTYPE_BF16 && dtype != FFA_DTYPE_F16 && dtype != FFA_DTYPE_F32) return FFA_ERR_UNSUPPORTED;
   if (Skv > 65535 * FWD_BN) return FFA_ERR_UNSUPPORTED;
+  // with a block mask a CTA records its kept key tiles in shared memory
+  if (block_mask && D == 192 && (Skv + FWD_BN - 1) / FWD_BN > FwdCfg<192, 128>::MAX_LIST) return FFA_ERR_UNSUPPORTED;
   if (block_mask && (n_br <= 0 || n_bc <= 0 || mask_bq <= 0 || mask_bkv <= 0 ||
                      (int64_t)n_br * mask_bq < Sq || (int64_t)n_bc * mask_bkv < Skv))
     return FFA_ERR_INVALID_ARG;
