@@ -715,6 +715,13 @@ def run_profile(args):
         o, lse = flash_fwd(q, k, v, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
         for _ in range(n):
             flash_bwd(do, q, k, v, o, lse, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
+    elif args.profile == "prefill192":
+        # config 5 prefill attention at (qk 192, v 128), B=2 (inputs 270 MB > L2)
+        q = torch.randn(2, 32, 4096, 192, device=dev).to(torch.bfloat16)
+        k = torch.randn(2, 32, 4096, 192, device=dev).to(torch.bfloat16)
+        v = torch.randn(2, 32, 4096, 128, device=dev).to(torch.bfloat16)
+        for _ in range(n):
+            flash_fwd(q, k, v, scale=192 ** -0.5, causal=True)
     elif args.profile == "fp32":
         # config 1: fp32 [2, 8, 1024, 64] causal forward + backward (CUDA-core kernels)
         q, k, v, do = (torch.randn(2, 8, 1024, 64, device=dev) for _ in range(4))
@@ -745,7 +752,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=["full", "small"], default="full")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
-    ap.add_argument("--profile", choices=["bwd", "decode", "mla", "fp32"], default=None,
+    ap.add_argument("--profile", choices=["bwd", "decode", "mla", "fp32", "prefill192"], default=None,
                     help="run only that kernel family a few times on a capture-sized case (for ncu)")
     ap.add_argument("--no-secondary", action="store_true", help="skip the other kernels' lines")
     args = ap.parse_args()
