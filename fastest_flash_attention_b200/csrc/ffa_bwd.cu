@@ -36,6 +36,7 @@
 #include "ffa_common.cuh"
 #include "ffa_host.h"
 
+#include <cstdlib>
 #include <type_traits>
 
 namespace ffa {
@@ -71,6 +72,9 @@ struct BwdParams {
   // the forward was given: masked pairs get P = 0 (nullptr: none)
   const uint8_t* block_mask;
   int n_br, n_bc, mask_bq, mask_bkv;
+  // CTA order: (b, kv head) pairs per group in dK/dV, (b, q head) pairs per
+  // group in dQ (whole GQA groups); see bwd_head_groups
+  int grp_kv, grp_q;
   ErrCtx ec;
 };
 
@@ -591,8 +595,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   // Key-tile-major order: under causal masking the first key tiles see the
   // most queries, so they are dispatched first.
   const int BHk = p.B * p.Hkv;
-  const int j = blockIdx.x / BHk;
-  const int bhk = blockIdx.x % BHk;
+  const int n_j = (p.Skv + BWD_BT - 1) / BWD_BT;
+  // (b, kv head) pairs in groups of p.grp_kv whose Q / dO stay in L2 while
+  // the group's key tiles stream them; within a group key tiles go in order
+  // (under causal masking the first ones see the most queries).
+  const int g0 = (int)(blockIdx.x / ((unsigned)p.grp_kv * n_j)) * p.grp_kv;
+  const int gn = min(p.grp_kv, BHk - g0);
+  const int rem = (int)blockIdx.x - g0 * n_j;
+  const int j = rem / gn;
+  const int bhk = g0 + rem % gn;
   const int b = bhk / p.Hkv, hkv = bhk % p.Hkv;
   const int group = p.Hq / p.Hkv;
   int i_lo, i_hi;
@@ -891,11 +902,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_q = (p.Sq + BWD_BT - 1) / BWD_BT;
-  // Query-tile-major order, heaviest (latest, under causal masking) first.
+  // (b, q head) pairs in groups of p.grp_q whose K / V stay in L2 while the
+  // group's query tiles stream them; within a group query tiles go heaviest
+  // (latest, under causal masking) first.
   const int BH = p.B * p.Hq;
-  const int ii = blockIdx.x / BH;
+  const int g0 = (int)(blockIdx.x / ((unsigned)p.grp_q * n_q)) * p.grp_q;
+  const int gn = min(p.grp_q, BH - g0);
+  const int rem = (int)blockIdx.x - g0 * n_q;
+  const int ii = rem / gn;
   const int i = p.causal ? (n_q - 1 - ii) : ii;
-  const int bh = blockIdx.x % BH;
+  const int bh = g0 + rem % gn;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int hkv = h / (p.Hq / p.Hkv);
   int j_lo, j_hi;
@@ -1094,6 +1110,34 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
+
+// CTA-order group sizes (see the kernels' block mapping): groups whose
+// streamed operands fit in about 48 MB of L2 together, so each streamed tile
+// is read from HBM once per group instead of once per CTA that reads it.
+// Sliding windows keep the plain order (a tile's readers are then near each
+// other in it anyway).  FFA_BWD_HEAD_GROUP=0 in the environment forces the
+// plain order (for measurements).
+static void bwd_head_groups(BwdParams& p, int D, int DV) {
+  static const int forced = [] {
+    const char* e = getenv("FFA_BWD_HEAD_GROUP");
+    return e ? atoi(e) : -1;
+  }();
+  const int G = p.Hq / p.Hkv;
+  const int BHk = p.B * p.Hkv, BH = p.B * p.Hq;
+  if (forced == 0 || (p.window > 0 && p.window < p.Skv)) {
+    p.grp_kv = BHk;
+    p.grp_q = BH;
+    return;
+  }
+  const double budget = 48.0 * 1024 * 1024;
+  const double qdo = (double)p.Sq * (D + DV) * 2.0 * G;  // Q and dO of a GQA group
+  const double kv = (double)p.Skv * (D + DV) * 2.0;      // K and V of a kv head
+  const int nk = (int)(budget / (qdo > 1 ? qdo : 1));
+  const int nq = (int)(budget / (kv > 1 ? kv : 1));
+  p.grp_kv = nk < 1 ? 1 : (nk > BHk ? BHk : nk);
+  p.grp_q = nq < 1 ? G : ((long long)nq * G > BH ? BH : nq * G);
+}
+
 template <typename T, int D, int DV, bool BM>
 static int launch_bwd(const CUtensorMap* maps, const BwdParams& p, const void* o, const void* dout,
                       const float* lse, float* lse2, float* delta, const int64_t* o_str, const int64_t* do_str,
@@ -1226,6 +1270,7 @@ extern "C" int ffa_bwd_masked(const void* dout, const void* q, const void* k, co
   p.mask_bkv = mask_bkv;
   p.ec.err = dev_err;
   p.ec.limit_ns = wait_limit_ns();
+  bwd_head_groups(p, D, Dv);
 
   const CUtensorMapDataType dt =
       dtype == FFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
