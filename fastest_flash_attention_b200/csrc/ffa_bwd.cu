@@ -1115,8 +1115,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // streamed operands fit in about 48 MB of L2 together, so each streamed tile
 // is read from HBM once per group instead of once per CTA that reads it.
 // Sliding windows keep the plain order (a tile's readers are then near each
-// other in it anyway).  FFA_BWD_HEAD_GROUP=0 in the environment forces the
-// plain order (for measurements).
+// other in it anyway).  FFA_BWD_HEAD_GROUP in the environment overrides it
+// (0: the plain order; N > 0: N kv heads per group; for measurements).
 static void bwd_head_groups(BwdParams& p, int D, int DV) {
   static const int forced = [] {
     const char* e = getenv("FFA_BWD_HEAD_GROUP");
@@ -1124,6 +1124,11 @@ static void bwd_head_groups(BwdParams& p, int D, int DV) {
   }();
   const int G = p.Hq / p.Hkv;
   const int BHk = p.B * p.Hkv, BH = p.B * p.Hq;
+  if (forced > 0) {  // kv heads per group
+    p.grp_kv = forced > BHk ? BHk : forced;
+    p.grp_q = p.grp_kv * G;
+    return;
+  }
   if (forced == 0 || (p.window > 0 && p.window < p.Skv)) {
     p.grp_kv = BHk;
     p.grp_q = BH;
