@@ -72,3 +72,27 @@ def test_config_defaults_match_reference():
     c = AttentionConfig()
     assert (c.block_size_q, c.block_size_kv, c.causal, c.page_size, c.pipeline_stages) == (0, 0, False, 64, 2)
     assert c.resolve_block_sizes(1024, 1024, 64) == (64, 64)
+
+
+def test_kernel_dtype_selection():
+    """fp32 (and fp64) inputs compute in fp32 unless compute_dtype asks for a
+    16-bit type; 16-bit inputs keep their type (cpu_reference.py:28-32)."""
+    from fastest_flash_attention_b200.attention import kernel_dtype, _ATTN_DTYPE_CODE
+    f32, f64 = torch.zeros(1, dtype=torch.float32), torch.zeros(1, dtype=torch.float64)
+    assert kernel_dtype(f32) == torch.float32
+    assert kernel_dtype(f64) == torch.float32
+    assert kernel_dtype(f32, torch.float16) == torch.float16
+    assert kernel_dtype(f32, torch.bfloat16) == torch.bfloat16
+    assert kernel_dtype(torch.zeros(1, dtype=torch.bfloat16), torch.float16) == torch.bfloat16
+    assert _ATTN_DTYPE_CODE == {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
+def test_fp32_entry_points_reject_misaligned_strides_without_launch():
+    """ffa_fwd with FFA_DTYPE_F32 validates 16-byte alignment and strides that
+    are multiples of 4 elements before touching the GPU."""
+    from fastest_flash_attention_b200 import _lib
+    lib = _lib.load()
+    s = _lib.i64arr(64 * 65, 64 * 65, 65)  # seq stride 65: not a multiple of 4 floats
+    st = lib.ffa_fwd(16, 16, 16, 16, None, 2, 1, 1, 1, 64, 64, 64, 64, s, s, s, s, 0.125, 0, 0, 0, 0.0,
+                     None, 0, 0, 64, 64, None, None)
+    assert st == 1  # FFA_ERR_INVALID_ARG
