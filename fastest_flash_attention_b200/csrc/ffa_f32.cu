@@ -87,6 +87,23 @@ __device__ __forceinline__ void f32_load_tile(float* dst, const float* src, int6
   }
 }
 
+// f32_load_tile through cp.async (16-byte copies, rows past `nrows` zero-filled):
+// the copies are in flight until cp_async_wait; a commit groups them.
+template <int W>
+__device__ __forceinline__ void f32_load_tile_async(float* dst, const float* src, int64_t rs, int r0, int nrows) {
+  constexpr int V4 = W / 4;
+  for (int idx = threadIdx.x; idx < 64 * V4; idx += F_THREADS) {
+    const int r = idx / V4, c = idx % V4;
+    const bool in = r0 + r < nrows;
+    const float* g = in ? src + (int64_t)(r0 + r) * rs + 4 * c : src;
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst + r * (W + 4) + 4 * c);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(g), "r"(in ? 16 : 0) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // acc[i][j] = sum_d A[4*ty + i][d] * Bm[tx + 16*j][d] over d < W (tiles of pitch W + 4).
 template <int W>
 __device__ __forceinline__ void f32_scores(const float* A, const float* Bm, int ty, int tx, float acc[4][4]) {
@@ -165,7 +182,10 @@ __device__ __forceinline__ float f32_score(const F32Params& p, float dot, float*
 
 template <int DQ, int DV>
 struct F32Smem {
-  static constexpr int FWD = (2 * 64 * (DQ + 4) + 64 * (DV + 4) + 64 * 68) * 4;
+  // forward: Q, P and NKV buffers of {K, V} (two, so the next tile loads
+  // during this one's math, where they fit)
+  static constexpr int NKV = (3 * 64 * (DQ + 4) + 2 * 64 * (DV + 4) + 64 * 68) * 4 <= 227 * 1024 ? 2 : 1;
+  static constexpr int FWD = (64 * (DQ + 4) + NKV * 64 * (DQ + DV + 8) + 64 * 68) * 4;
   static constexpr int DKDV = (2 * 64 * (DQ + 4) + 2 * 64 * (DV + 4) + 2 * 64 * 68 + 2 * 64) * 4;
   static constexpr int DQK = (2 * 64 * (DQ + 4) + 2 * 64 * (DV + 4) + 64 * 68) * 4;
 };
@@ -173,11 +193,12 @@ struct F32Smem {
 // Forward: one CTA per (64-query tile, query head, batch).
 template <int DQ, int DV>
 __global__ void __launch_bounds__(F_THREADS) ffa_f32_fwd_kernel(const F32Params p) {
+  constexpr int NKV = F32Smem<DQ, DV>::NKV;
   extern __shared__ float4 f32_smem4[];
   float* sQ = reinterpret_cast<float*>(f32_smem4);
-  float* sK = sQ + 64 * (DQ + 4);
-  float* sV = sK + 64 * (DQ + 4);
-  float* sP = sV + 64 * (DV + 4);
+  float* sP = sQ + 64 * (DQ + 4);
+  float* sKV = sP + 64 * 68;  // buffer u: K at u * KV_STRIDE, V after it
+  constexpr int KV_STRIDE = 64 * (DQ + DV + 8);
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
   const int ty = threadIdx.x / 16, tx = threadIdx.x % 16;
@@ -185,7 +206,7 @@ __global__ void __launch_bounds__(F_THREADS) ffa_f32_fwd_kernel(const F32Params 
   const float* qb = p.q + b * p.q_s[0] + h * p.q_s[1];
   const float* kb = p.k + b * p.k_s[0] + hk * p.k_s[1];
   const float* vb = p.v + b * p.v_s[0] + hk * p.v_s[1];
-  f32_load_tile<DQ>(sQ, qb, p.q_s[2], i0, p.Sq);
+  f32_load_tile_async<DQ>(sQ, qb, p.q_s[2], i0, p.Sq);
 
   float m[4], l[4];
   float4 acc[4][DV / 64];
@@ -198,11 +219,31 @@ __global__ void __launch_bounds__(F_THREADS) ffa_f32_fwd_kernel(const F32Params 
   }
   int klo, khi;
   f32_key_range(p, i0, i1, klo, khi);
-  for (int kt = max(klo, 0) / F_BN; kt * F_BN < khi; ++kt) {
+  const int kt0 = max(klo, 0) / F_BN;
+  if (kt0 * F_BN < khi) {
+    f32_load_tile_async<DQ>(sKV, kb, p.k_s[2], kt0 * F_BN, p.Skv);
+    f32_load_tile_async<DV>(sKV + 64 * (DQ + 4), vb, p.v_s[2], kt0 * F_BN, p.Skv);
+  }
+  cp_async_commit();  // Q and the first K / V tile
+  for (int kt = kt0; kt * F_BN < khi; ++kt) {
     const int j0 = kt * F_BN;
-    __syncthreads();  // previous tile's sK / sV / sP reads are done
-    f32_load_tile<DQ>(sK, kb, p.k_s[2], j0, p.Skv);
-    f32_load_tile<DV>(sV, vb, p.v_s[2], j0, p.Skv);
+    float* sK = sKV + ((kt - kt0) % NKV) * KV_STRIDE;
+    float* sV = sK + 64 * (DQ + 4);
+    __syncthreads();  // the previous tile's reads (of sP and of the buffer refilled next) are done
+    if (NKV == 2 && (kt + 1) * F_BN < khi) {
+      float* nK = sKV + ((kt + 1 - kt0) % 2) * KV_STRIDE;
+      f32_load_tile_async<DQ>(nK, kb, p.k_s[2], j0 + F_BN, p.Skv);
+      f32_load_tile_async<DV>(nK + 64 * (DQ + 4), vb, p.v_s[2], j0 + F_BN, p.Skv);
+      cp_async_commit();
+      cp_async_wait<1>();  // all but the tile just requested
+    } else {
+      if (NKV == 1 && kt > kt0) {
+        f32_load_tile_async<DQ>(sK, kb, p.k_s[2], j0, p.Skv);
+        f32_load_tile_async<DV>(sV, vb, p.v_s[2], j0, p.Skv);
+        cp_async_commit();
+      }
+      cp_async_wait<0>();
+    }
     __syncthreads();
     float s[4][4];
     f32_scores<DQ>(sQ, sK, ty, tx, s);
@@ -240,6 +281,7 @@ __global__ void __launch_bounds__(F_THREADS) ffa_f32_fwd_kernel(const F32Params 
     __syncthreads();
     f32_accumulate<DV>(sP, sV, ty, tx, acc);
   }
+  cp_async_wait<0>();  // no copy may still target shared memory when the CTA exits
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int qi = i0 + 4 * ty + i;
