@@ -716,10 +716,11 @@ def run_profile(args):
         for _ in range(n):
             flash_bwd(do, q, k, v, o, lse, scale=D ** -0.5, causal=True, window=1024, softcap=30.0)
     elif args.profile == "prefill192":
-        # config 5 prefill attention at (qk 192, v 128), B=2 (inputs 270 MB > L2)
-        q = torch.randn(2, 32, 4096, 192, device=dev).to(torch.bfloat16)
-        k = torch.randn(2, 32, 4096, 192, device=dev).to(torch.bfloat16)
-        v = torch.randn(2, 32, 4096, 128, device=dev).to(torch.bfloat16)
+        # config 5 prefill attention at (qk 192, v 128), B=4 (inputs 540 MB > L2; 2048 CTAs, the
+        # L2-grouped CTA order as at B=16)
+        q = torch.randn(4, 32, 4096, 192, device=dev).to(torch.bfloat16)
+        k = torch.randn(4, 32, 4096, 192, device=dev).to(torch.bfloat16)
+        v = torch.randn(4, 32, 4096, 128, device=dev).to(torch.bfloat16)
         for _ in range(n):
             flash_fwd(q, k, v, scale=192 ** -0.5, causal=True)
     elif args.profile == "fp32":

@@ -671,7 +671,7 @@ static int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
 // refetching them from HBM; whole GQA groups per group.  FFA_FWD_HEAD_GROUP in
 // the environment overrides the group size (for measurements; 0 = all heads
 // in one group, the plain heaviest-first order).
-static int fwd_head_group(int BH, int G, int Skv, int D, int Dv, int window) {
+static int fwd_head_group(int BH, int G, int Skv, int D, int Dv, int window, long long ctas) {
   static const int forced = [] {
     const char* e = getenv("FFA_FWD_HEAD_GROUP");
     return e ? atoi(e) : -1;
@@ -682,6 +682,13 @@ static int fwd_head_group(int BH, int G, int Skv, int D, int Dv, int window) {
   // the same query block of every head together keeps within L2: the plain
   // order (measured 0.486-0.491 ms on config 3 against 0.495 grouped).
   if (window > 0 && window < Skv) return BH;
+  // A short grid keeps the plain order too: with few waves, the heaviest
+  // query blocks of the last group would start near the end and set the
+  // tail (qk 192, B=2: 1024 CTAs, 0.385 ms plain against 0.422 grouped; B=4,
+  // 2048 CTAs: 0.779 against 0.740).
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (ctas < 10LL * sms) return BH;
   const double kv_per_group = (double)Skv * (D + Dv) * 2.0;  // one kv head's K and V
   int kv_heads = (int)(48.0 * 1024 * 1024 / (kv_per_group > 1 ? kv_per_group : 1));
   if (kv_heads < 1) kv_heads = 1;
@@ -750,7 +757,7 @@ extern "C" int ffa_fwd(const void* q, const void* k, const void* v, void* o, flo
   p.q_offset = q_offset;
   const int nqt = fwd_query_tiles(D, Sq, Skv, causal, window, block_mask != nullptr);
   p.n_qblk = (Sq + FWD_BM * nqt - 1) / (FWD_BM * nqt);
-  p.head_group = fwd_head_group(B * Hq, Hq / Hkv, Skv, D, Dv, window);
+  p.head_group = fwd_head_group(B * Hq, Hq / Hkv, Skv, D, Dv, window, (long long)p.n_qblk * B * Hq);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.use_softcap = softcap > 0.f;
   p.sc_pre = p.use_softcap ? scale / softcap : 0.f;
