@@ -1141,6 +1141,12 @@ static void bwd_head_groups(BwdParams& p, int D, int DV) {
   const int nq = (int)(budget / (kv > 1 ? kv : 1));
   p.grp_kv = nk < 1 ? 1 : (nk > BHk ? BHk : nk);
   p.grp_q = nq < 1 ? G : ((long long)nq * G > BH ? BH : nq * G);
+  // Short grids (under 10 waves) keep the plain order, as the forward does:
+  // the heaviest tiles of the last group would otherwise start near the end.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if ((long long)(p.Skv + BWD_BT - 1) / BWD_BT * BHk < 10LL * sms) p.grp_kv = BHk;
+  if ((long long)(p.Sq + BWD_BT - 1) / BWD_BT * BH < 10LL * sms) p.grp_q = BH;
 }
 
 template <typename T, int D, int DV, bool BM>
